@@ -1,0 +1,216 @@
+"""MIT2 weight-bundle writer and reader for the IndexTTS 2.5 GPT (UnifiedVoice).
+
+The container format is the one the reference parses in
+``vendor/metal-runtime/bundle.cpp:176-293`` and ``src/weights.cpp:11-27``:
+
+* ``manifest.json``: ``format "MIT2"``, ``version 1``, ``alignment``,
+  ``endianness "little"``, ``target "index-tts2.5"`` and a ``tensors`` array of
+  ``{name, shape, dtype "f32", offset, nbytes}``.  The reference parser slices the
+  tensors array from the first ``[`` after ``"tensors"`` to the LAST ``]`` of the
+  file (``bundle.cpp:71-98``), so ``tensors`` is written as the final key.
+* ``weights.bin``: ``"MIT2"`` + u32 version + u32 alignment, then every tensor
+  at an offset that is a multiple of ``alignment`` (``bundle.cpp:233-283``).
+
+``write_synthetic_gpt_bundle`` emits the random-init GPT used by the tests and
+the benchmark (no real checkpoint exists on this machine).  Shapes follow the
+checks in ``src/gpt.cpp:8-23`` (Conv1D weights in HF ``[in, out]`` layout,
+``mel_head`` and ``spk_emb_proj`` in ``nn.Linear`` ``[out, in]`` layout).
+
+Initialisation: every matrix, embedding and bias ~ N(0, 0.02); LayerNorm
+gamma = 1 + N(0, 0.02) and beta ~ N(0, 0.02) (perturbed away from GPT-2's
+1/0 so that the gamma/beta paths are exercised).  Each tensor draws from its own
+numpy PCG64 stream seeded by ``(seed, tensor index)``, so a bundle is a pure
+function of its arguments and is re-created bit-identically on any machine
+with the same numpy.  ``mask_stop`` sets ``mel_head.bias[8193] = -1e30`` so a
+decode never emits the stop code and always runs to its requested length.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import re
+import struct
+from dataclasses import dataclass
+
+import numpy as np
+
+WIDTH = 1280
+HEADS = 20
+HEAD_DIM = 64
+FFN = 5120
+MEL_VOCAB = 8194
+TEXT_VOCAB = 60510
+LANGS = 107
+SPK_DIM = 192
+TEXT_POS_ROWS = 602
+MEL_POS_ROWS = 1818
+STOP_CODE = 8193
+START_CODE = 8192
+
+
+def gpt_tensor_specs(layers: int, mel_pos_rows: int = MEL_POS_ROWS,
+                     text_pos_rows: int = TEXT_POS_ROWS):
+    """Ordered (name, shape, kind) list; kind in {"mat", "bias", "ln_w", "ln_b"}."""
+    specs = [
+        ("gpt.spk_emb_proj.weight", (WIDTH, SPK_DIM), "mat"),
+        ("gpt.spk_emb_proj.bias", (WIDTH,), "bias"),
+        ("gpt.text_embedding.weight", (TEXT_VOCAB, WIDTH), "mat"),
+        ("gpt.text_pos_embedding.emb.weight", (text_pos_rows, WIDTH), "mat"),
+        ("gpt.lang_embedding.weight", (LANGS, WIDTH), "mat"),
+        ("gpt.mel_embedding.weight", (MEL_VOCAB, WIDTH), "mat"),
+        ("gpt.mel_pos_embedding.emb.weight", (mel_pos_rows, WIDTH), "mat"),
+    ]
+    for i in range(layers):
+        p = f"gpt.gpt.h.{i}"
+        specs += [
+            (f"{p}.ln_1.weight", (WIDTH,), "ln_w"),
+            (f"{p}.ln_1.bias", (WIDTH,), "ln_b"),
+            (f"{p}.attn.c_attn.weight", (WIDTH, 3 * WIDTH), "mat"),
+            (f"{p}.attn.c_attn.bias", (3 * WIDTH,), "bias"),
+            (f"{p}.attn.c_proj.weight", (WIDTH, WIDTH), "mat"),
+            (f"{p}.attn.c_proj.bias", (WIDTH,), "bias"),
+            (f"{p}.ln_2.weight", (WIDTH,), "ln_w"),
+            (f"{p}.ln_2.bias", (WIDTH,), "ln_b"),
+            (f"{p}.mlp.c_fc.weight", (WIDTH, FFN), "mat"),
+            (f"{p}.mlp.c_fc.bias", (FFN,), "bias"),
+            (f"{p}.mlp.c_proj.weight", (FFN, WIDTH), "mat"),
+            (f"{p}.mlp.c_proj.bias", (WIDTH,), "bias"),
+        ]
+    specs += [
+        ("gpt.gpt.ln_f.weight", (WIDTH,), "ln_w"),
+        ("gpt.gpt.ln_f.bias", (WIDTH,), "ln_b"),
+        ("gpt.final_norm.weight", (WIDTH,), "ln_w"),
+        ("gpt.final_norm.bias", (WIDTH,), "ln_b"),
+        ("gpt.mel_head.weight", (MEL_VOCAB, WIDTH), "mat"),
+        ("gpt.mel_head.bias", (MEL_VOCAB,), "bias"),
+    ]
+    return specs
+
+
+def _tensor_values(seed: int, index: int, shape, kind: str, std: float):
+    rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, index])))
+    v = rng.standard_normal(int(np.prod(shape)), dtype=np.float32)
+    v *= np.float32(std)
+    if kind == "ln_w":
+        v += np.float32(1.0)
+    return v
+
+
+def bundle_complete(path: str) -> bool:
+    return os.path.exists(os.path.join(path, "manifest.json")) and \
+        os.path.exists(os.path.join(path, ".complete"))
+
+
+def write_synthetic_gpt_bundle(path: str, *, seed: int = 42, layers: int = 24,
+                               mask_stop: bool = False, std: float = 0.02,
+                               mel_pos_rows: int = MEL_POS_ROWS,
+                               alignment: int = 256, reuse: bool = True) -> str:
+    """Write a random-init GPT bundle to ``path`` (a directory) and return the
+    SHA-256 of ``weights.bin``.  An existing complete bundle written with the same
+    arguments is reused (its recorded hash is returned)."""
+    args = dict(seed=seed, layers=layers, mask_stop=bool(mask_stop), std=std,
+                mel_pos_rows=mel_pos_rows, alignment=alignment)
+    os.makedirs(path, exist_ok=True)
+    marker = os.path.join(path, ".complete")
+    if reuse and bundle_complete(path):
+        with open(marker) as f:
+            rec = json.load(f)
+        if rec.get("args") == args:
+            return rec["sha256"]
+    if os.path.exists(marker):
+        os.remove(marker)
+    specs = gpt_tensor_specs(layers, mel_pos_rows)
+    records = []
+    offset = alignment
+    h = hashlib.sha256()
+    with open(os.path.join(path, "weights.bin"), "wb") as f:
+        header = b"MIT2" + struct.pack("<II", 1, alignment)
+        header += b"\0" * (alignment - len(header))
+        f.write(header)
+        h.update(header)
+        for idx, (name, shape, kind) in enumerate(specs):
+            v = _tensor_values(seed, idx, shape, kind, std)
+            if mask_stop and name == "gpt.mel_head.bias":
+                v[STOP_CODE] = np.float32(-1e30)
+            raw = v.tobytes()
+            f.write(raw)
+            h.update(raw)
+            records.append({"name": name, "shape": list(shape), "dtype": "f32",
+                            "offset": offset, "nbytes": len(raw), "component": "gpt"})
+            offset += len(raw)
+            pad = (-offset) % alignment
+            if pad:
+                f.write(b"\0" * pad)
+                h.update(b"\0" * pad)
+                offset += pad
+    manifest = {"format": "MIT2", "version": 1, "alignment": alignment,
+                "endianness": "little", "target": "index-tts2.5",
+                "weights_file": "weights.bin",
+                "synthetic": {"seed": seed, "layers": layers, "std": std,
+                              "mask_stop": bool(mask_stop), "init": "normal"},
+                "tensors": records}
+    with open(os.path.join(path, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=0)
+    digest = h.hexdigest()
+    with open(marker, "w") as f:
+        json.dump({"args": args, "sha256": digest}, f)
+    return digest
+
+
+@dataclass
+class TensorRecord:
+    name: str
+    shape: tuple
+    dtype: str
+    offset: int
+    nbytes: int
+
+
+class Bundle:
+    """Read-only numpy view of an MIT2 bundle directory (memory-mapped)."""
+
+    def __init__(self, path: str):
+        with open(os.path.join(path, "manifest.json")) as f:
+            self.manifest = json.load(f)
+        if self.manifest.get("format") != "MIT2":
+            raise ValueError("not an MIT2 bundle")
+        self.data = np.memmap(os.path.join(path, self.manifest.get("weights_file", "weights.bin")),
+                              dtype=np.uint8, mode="r")
+        self.tensors = {}
+        for t in self.manifest["tensors"]:
+            self.tensors[t["name"]] = TensorRecord(t["name"], tuple(t["shape"]), t["dtype"],
+                                                   int(t["offset"]), int(t["nbytes"]))
+
+    def get(self, name: str) -> np.ndarray:
+        t = self.tensors[name]
+        dt = {"f32": np.float32, "u32": np.uint32}[t.dtype]
+        return self.data[t.offset:t.offset + t.nbytes].view(dt).reshape(t.shape)
+
+    def layers(self) -> int:
+        pat = re.compile(r"^gpt\.gpt\.h\.(\d+)\.ln_1\.weight$")
+        return sum(1 for n in self.tensors if pat.match(n))
+
+
+def write_fixture_bundle(path: str, f32: dict, u32: dict | None = None, alignment: int = 64):
+    """Small fixture bundle (no ``target`` check) in the same container format."""
+    os.makedirs(path, exist_ok=True)
+    records, offset, blobs = [], alignment, []
+    items = [(k, np.ascontiguousarray(v, dtype=np.float32), "f32") for k, v in f32.items()]
+    items += [(k, np.ascontiguousarray(v, dtype=np.uint32), "u32") for k, v in (u32 or {}).items()]
+    for name, arr, dt in items:
+        raw = arr.tobytes()
+        records.append({"name": name, "shape": list(arr.shape) or [1], "dtype": dt,
+                        "offset": offset, "nbytes": len(raw)})
+        blobs.append((offset, raw))
+        offset += len(raw) + ((-len(raw)) % alignment)
+    with open(os.path.join(path, "weights.bin"), "wb") as f:
+        head = b"MIT2" + struct.pack("<II", 1, alignment)
+        f.write(head + b"\0" * (alignment - len(head)))
+        for off, raw in blobs:
+            f.seek(off)
+            f.write(raw)
+        f.truncate(offset)
+    with open(os.path.join(path, "manifest.json"), "w") as f:
+        json.dump({"format": "MIT2", "version": 1, "alignment": alignment,
+                   "endianness": "little", "tensors": records}, f)
