@@ -1,0 +1,115 @@
+// Shared device-side definitions for the B200 GPT decoder.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "model.hpp"
+
+namespace itts {
+
+// Model dimensions of the IndexTTS 2.5 UnifiedVoice GPT (src/gpt.cpp:7-23).
+constexpr int kWidth = 1280;
+constexpr int kHeads = 20;
+constexpr int kHeadDim = 64;
+constexpr int kQkv = 3 * kWidth;
+constexpr int kFfn = 5120;
+constexpr int kVocab = 8194;
+constexpr int kStopCode = 8193;
+constexpr int kStartCode = 8192;
+constexpr int kKvCapacity = 4096;
+constexpr int kMaxLayers = 24;
+constexpr int kMaxPrefix = 1024;
+constexpr float kLnEps = 1e-5f;
+
+// Decode kernels run 512 threads (16 warps) per CTA, one CTA per SM.
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+
+// Wall-clock limit of every device-side spin-wait.  A legitimate wait lasts
+// microseconds; the limit only turns a lost peer into an error status.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_volatile(const int* p) {
+    return *reinterpret_cast<const volatile int*>(p);
+}
+
+// Weights are streamed once per decode step: read-only loads without L1 allocation.
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    acc = fmaf(a.w, b.w, acc);
+    return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum over all threads of the CTA; `red` holds >= 32 floats.
+// Every thread receives the total.  Contains two __syncthreads().
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < (int)(blockDim.x >> 5) ? red[lane] : -INFINITY;
+    return warp_max(t);
+}
+
+__device__ __forceinline__ void set_status(int* status, int code, int where, int detail) {
+    if (atomicCAS(status, 0, code) == 0) {
+        status[1] = where;
+        status[2] = blockIdx.x;
+        status[3] = detail;
+    }
+}
+
+// tanh GELU with the clamps of mit2_gelu_f32 (kernels.metal:486-503).
+__device__ __forceinline__ float gelu_ref(float v) {
+    if (v > 10.0f) return v;
+    if (v < -10.0f) return 0.0f;
+    return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
+
+}  // namespace itts

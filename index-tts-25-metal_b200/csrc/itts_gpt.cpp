@@ -1,0 +1,946 @@
+// Host runtime of the B200 GPT decoder: implements include/itts_gpt.h.
+//
+// Mirrors the reference's GptDecoder (src/gpt.cpp, src/gpt_sampling.cpp):
+// the same argument checks and error classes, the same generation loop
+// semantics (history seeded with {1, 8192}, first generated code at mel
+// position 2, stop code 8193, codes >= 8192 rejected), the same beam-search
+// bookkeeping.  All tensor math runs on the device (decode.cu, prefill.cu,
+// misc.cu); the host owns validation, memory and launch order.
+#include "itts_gpt.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <new>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "mit2_bundle.hpp"
+#include "model.hpp"
+
+namespace itts {
+cudaError_t launch_beam_scores(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
+                               float beam_score, float* tmp, float* out, int* status, cudaStream_t s);
+}
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct Failure {
+    int code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Failure{code, msg}; }
+[[noreturn]] void invalid(const std::string& msg) { fail(ITTS_ERR_INVALID_ARGUMENT, msg); }
+
+void ck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(e == cudaErrorMemoryAllocation ? ITTS_ERR_OUT_OF_MEMORY : ITTS_ERR_CUDA,
+             std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+constexpr uint32_t kW = 1280, kVocab = 8194, kCap = 4096, kH = 20, kHd = 64;
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+template <class T>
+T* dev_alloc(size_t count, const char* what) {
+    void* p = nullptr;
+    ck(cudaMalloc(&p, count * sizeof(T)), what);
+    return static_cast<T*>(p);
+}
+
+}  // namespace
+
+struct itts_gpt_state {
+    int device = 0;
+    uint32_t tokens = 0, layers = 0;
+    float* d = nullptr;  // [layer][K|V][head][tokens][64]
+    ~itts_gpt_state() {
+        if (d) {
+            int cur = 0;
+            cudaGetDevice(&cur);
+            cudaSetDevice(device);
+            cudaFree(d);
+            cudaSetDevice(cur);
+        }
+    }
+};
+
+struct itts_gpt_ctx {
+    int device = 0, dtype = 0, sm_count = 0, mode = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    uint32_t layers = 0, mel_pos_rows = 0, text_pos_rows = 0;
+    char* d_weights = nullptr;
+    size_t weight_bytes = 0;
+    uint64_t stream_bytes = 0;
+    itts::ModelW hw{};
+    itts::ModelW* d_model = nullptr;
+    const float *spk_w = nullptr, *spk_b = nullptr, *text_emb = nullptr, *text_pos = nullptr, *lang_emb = nullptr;
+    float* d_kv = nullptr;
+    float *d_hidden = nullptr, *d_x = nullptr, *d_qkv = nullptr, *d_att = nullptr, *d_r = nullptr, *d_ff = nullptr;
+    float* d_act = nullptr;
+    itts::DecodeBuffers db{};
+    uint32_t* d_history = nullptr;  // {1, 8192}
+    uint32_t* d_codes = nullptr;    // [kCap]
+    uint32_t* d_info = nullptr;     // [4]
+    float* d_misc = nullptr;        // prepare inputs / processor buffers
+    uint32_t* d_hist = nullptr;     // processor history (grown on demand)
+    size_t d_hist_cap = 0;
+    float* d_beam = nullptr;        // beam logits slots + scores
+    uint32_t beam_cap = 0;
+    float* h_stage = nullptr;       // pinned [1024 * 1280]
+    float* h_logits = nullptr;      // pinned [8194 * 10]
+    uint32_t* h_codes = nullptr;    // pinned [kCap]
+    itts::DecodeCtl* h_ctl = nullptr;
+    uint32_t cached = 0, prefix_rows = 0;
+    bool have_prefill = false;
+    uint64_t launches = 0;
+    bool pending = false;           // an async decode has not been synced yet
+    uint32_t* pending_info = nullptr;
+
+    ~itts_gpt_ctx() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (void* p : {(void*)d_weights, (void*)d_model, (void*)d_kv, (void*)d_hidden, (void*)d_act,
+                        (void*)d_history, (void*)d_codes, (void*)d_info, (void*)d_misc, (void*)d_hist,
+                        (void*)d_beam})
+            if (p) cudaFree(p);
+        for (void* p : {(void*)h_stage, (void*)h_logits, (void*)h_codes, (void*)h_ctl})
+            if (p) cudaFreeHost(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+template <class F>
+int guard(itts_gpt_ctx* ctx, F&& f, bool set_device = true) {
+    try {
+        if (ctx && set_device) ck(cudaSetDevice(ctx->device), "cudaSetDevice");
+        f();
+        return ITTS_OK;
+    } catch (const Failure& e) {
+        if (ctx) ctx->err = e.msg;
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        if (ctx) ctx->err = "host allocation failed";
+        return ITTS_ERR_OUT_OF_MEMORY;
+    } catch (const std::invalid_argument& e) {
+        if (ctx) ctx->err = e.what();
+        return ITTS_ERR_INVALID_ARGUMENT;
+    } catch (const std::exception& e) {
+        if (ctx) ctx->err = e.what();
+        return ITTS_ERR_RUNTIME;
+    }
+}
+
+// ---------------------------------------------------------------- loading
+// src/weights.cpp:11-27 and src/gpt.cpp:8-23: container, target and shape
+// checks.  Host only, so malformed bundles are rejected before any CUDA call.
+void validate_bundle(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
+    if (b.target() != "index-tts2.5") fail(ITTS_ERR_RUNTIME, "Expected an IndexTTS 2.5 model bundle");
+    b.check_sizes();
+    auto shape = [&](const std::string& n, std::vector<int64_t> want) {
+        if (b.info(n).shape != want) fail(ITTS_ERR_RUNTIME, "Unsupported 2.5 GPT shape: " + n);
+    };
+    // gpt.cpp:8-23
+    shape("gpt.spk_emb_proj.weight", {1280, 192});
+    shape("gpt.text_embedding.weight", {60510, 1280});
+    shape("gpt.lang_embedding.weight", {107, 1280});
+    shape("gpt.mel_embedding.weight", {8194, 1280});
+    uint32_t layers = 0;
+    while (layers < 24 && b.find("gpt.gpt.h." + std::to_string(layers) + ".ln_1.weight")) ++layers;
+    if (!layers) fail(ITTS_ERR_RUNTIME, "bundle has no GPT layers");
+    const char* conv[4] = {"attn.c_attn", "attn.c_proj", "mlp.c_fc", "mlp.c_proj"};
+    const std::vector<int64_t> conv_shape[4] = {{1280, 3840}, {1280, 1280}, {1280, 5120}, {5120, 1280}};
+    for (uint32_t i = 0; i < layers; ++i)
+        for (int k = 0; k < 4; ++k) shape("gpt.gpt.h." + std::to_string(i) + "." + conv[k] + ".weight", conv_shape[k]);
+    auto vec = [&](const std::string& n, int64_t len) { shape(n, {len}); };
+    for (uint32_t i = 0; i < layers; ++i) {
+        const std::string p = "gpt.gpt.h." + std::to_string(i);
+        vec(p + ".ln_1.weight", 1280);
+        vec(p + ".ln_1.bias", 1280);
+        vec(p + ".ln_2.weight", 1280);
+        vec(p + ".ln_2.bias", 1280);
+        vec(p + ".attn.c_attn.bias", 3840);
+        vec(p + ".attn.c_proj.bias", 1280);
+        vec(p + ".mlp.c_fc.bias", 5120);
+        vec(p + ".mlp.c_proj.bias", 1280);
+    }
+    for (const char* n : {"gpt.gpt.ln_f.weight", "gpt.gpt.ln_f.bias", "gpt.final_norm.weight", "gpt.final_norm.bias"})
+        vec(n, 1280);
+    vec("gpt.spk_emb_proj.bias", 1280);
+    shape("gpt.mel_head.weight", {8194, 1280});
+    vec("gpt.mel_head.bias", 8194);
+    const auto& mp = b.info("gpt.mel_pos_embedding.emb.weight");
+    const auto& tp = b.info("gpt.text_pos_embedding.emb.weight");
+    if (mp.shape.size() != 2 || mp.shape[1] != 1280 || mp.shape[0] < 3)
+        fail(ITTS_ERR_RUNTIME, "Unsupported 2.5 GPT shape: gpt.mel_pos_embedding.emb.weight");
+    if (tp.shape.size() != 2 || tp.shape[1] != 1280)
+        fail(ITTS_ERR_RUNTIME, "Unsupported 2.5 GPT shape: gpt.text_pos_embedding.emb.weight");
+    c->layers = layers;
+    c->mel_pos_rows = uint32_t(mp.shape[0]);
+    c->text_pos_rows = uint32_t(tp.shape[0]);
+}
+
+void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
+    const uint32_t layers = c->layers;
+    // device layout: every tensor 256-byte aligned in one allocation
+    std::vector<std::pair<const itts::TensorInfo*, size_t>> plan;
+    size_t total = 0;
+    auto add = [&](const std::string& n) {
+        const auto* t = &b.info(n);
+        plan.emplace_back(t, total);
+        total += align256(t->nbytes);
+        return plan.size() - 1;
+    };
+    std::vector<size_t> idx;
+    for (const char* n : {"gpt.spk_emb_proj.weight", "gpt.spk_emb_proj.bias", "gpt.text_embedding.weight",
+                          "gpt.text_pos_embedding.emb.weight", "gpt.lang_embedding.weight",
+                          "gpt.mel_embedding.weight", "gpt.mel_pos_embedding.emb.weight", "gpt.gpt.ln_f.weight",
+                          "gpt.gpt.ln_f.bias", "gpt.final_norm.weight", "gpt.final_norm.bias",
+                          "gpt.mel_head.weight", "gpt.mel_head.bias"})
+        idx.push_back(add(n));
+    const char* per_layer[12] = {"ln_1.weight", "ln_1.bias", "attn.c_attn.weight", "attn.c_attn.bias",
+                                 "attn.c_proj.weight", "attn.c_proj.bias", "ln_2.weight", "ln_2.bias",
+                                 "mlp.c_fc.weight", "mlp.c_fc.bias", "mlp.c_proj.weight", "mlp.c_proj.bias"};
+    for (uint32_t i = 0; i < layers; ++i)
+        for (const char* n : per_layer) idx.push_back(add("gpt.gpt.h." + std::to_string(i) + "." + n));
+    c->d_weights = dev_alloc<char>(total, "weight allocation");
+    c->weight_bytes = total;
+
+    // upload; Conv1D matrices go through a staging buffer and a transpose
+    float* stage = dev_alloc<float>(size_t(5120) * 1280, "transpose staging");
+    try {
+        for (const auto& pe : plan) {
+            const itts::TensorInfo& t = *pe.first;
+            char* dst = c->d_weights + pe.second;
+            const bool is_conv = t.name.rfind("gpt.gpt.h.", 0) == 0 && t.shape.size() == 2;
+            if (is_conv) {
+                ck(cudaMemcpy(stage, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+                ck(itts::launch_transpose(stage, reinterpret_cast<float*>(dst), int(t.shape[0]), int(t.shape[1]),
+                                          nullptr),
+                   "transpose launch");
+                ck(cudaDeviceSynchronize(), "transpose");
+            } else {
+                ck(cudaMemcpy(dst, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+            }
+        }
+    } catch (...) {
+        cudaFree(stage);
+        throw;
+    }
+    cudaFree(stage);
+    auto ptr = [&](size_t i) { return reinterpret_cast<const float*>(c->d_weights + plan[idx[i]].second); };
+    c->spk_w = ptr(0);
+    c->spk_b = ptr(1);
+    c->text_emb = ptr(2);
+    c->text_pos = ptr(3);
+    c->lang_emb = ptr(4);
+    c->hw.mel_emb = ptr(5);
+    c->hw.mel_pos = ptr(6);
+    c->hw.lnf_g = ptr(7);
+    c->hw.lnf_b = ptr(8);
+    c->hw.fn_g = ptr(9);
+    c->hw.fn_b = ptr(10);
+    c->hw.w_head = ptr(11);
+    c->hw.b_head = ptr(12);
+    c->hw.layers = int(layers);
+    for (uint32_t i = 0; i < layers; ++i) {
+        const size_t o = 13 + size_t(i) * 12;
+        itts::LayerW& L = c->hw.layer[i];
+        L.ln1_g = ptr(o + 0);
+        L.ln1_b = ptr(o + 1);
+        L.w_qkv = ptr(o + 2);
+        L.b_qkv = ptr(o + 3);
+        L.w_o = ptr(o + 4);
+        L.b_o = ptr(o + 5);
+        L.ln2_g = ptr(o + 6);
+        L.ln2_b = ptr(o + 7);
+        L.w_fc = ptr(o + 8);
+        L.b_fc = ptr(o + 9);
+        L.w_mp = ptr(o + 10);
+        L.b_mp = ptr(o + 11);
+    }
+    const uint64_t per_layer_floats = 19660800ull + 11520ull + 5120ull;
+    c->stream_bytes = 4ull * (per_layer_floats * layers + 10488320ull + 8194ull + 5120ull + 2560ull);
+}
+
+void alloc_buffers(itts_gpt_ctx* c) {
+    const size_t kv_floats = size_t(c->layers) * 2 * kH * kCap * kHd;
+    c->d_kv = dev_alloc<float>(kv_floats, "KV cache allocation");
+    const size_t T = 1024;
+    const size_t pre = T * kW * 4 + T * 3840 + T * 5120;  // hidden, x, att, r + qkv + ff
+    c->d_hidden = dev_alloc<float>(pre, "prefill scratch");
+    c->d_x = c->d_hidden + T * kW;
+    c->d_att = c->d_x + T * kW;
+    c->d_r = c->d_att + T * kW;
+    c->d_qkv = c->d_r + T * kW;
+    c->d_ff = c->d_qkv + T * 3840;
+    // decode activations (each region 256-byte aligned)
+    const size_t sizes[8] = {kW, 3840, kW, kW, 5120, 8448, size_t(kH) * 128 * 66, 64};
+    size_t total = 0;
+    for (size_t s : sizes) total += align256(s * 4);
+    c->d_act = reinterpret_cast<float*>(dev_alloc<char>(total, "decode buffers"));
+    char* p = reinterpret_cast<char*>(c->d_act);
+    float* regions[8];
+    for (int i = 0; i < 8; ++i) {
+        regions[i] = reinterpret_cast<float*>(p);
+        p += align256(sizes[i] * 4);
+    }
+    c->db.kv = c->d_kv;
+    c->db.h = regions[0];
+    c->db.qkv = regions[1];
+    c->db.attn = regions[2];
+    c->db.r = regions[3];
+    c->db.ff = regions[4];
+    c->db.logits = regions[5];
+    c->db.part = regions[6];
+    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[7]);
+    ck(cudaMemset(c->d_act, 0, total), "decode buffer init");
+    c->d_history = dev_alloc<uint32_t>(2, "history");
+    const uint32_t hist[2] = {1, 8192};
+    ck(cudaMemcpy(c->d_history, hist, sizeof hist, cudaMemcpyHostToDevice), "history upload");
+    c->d_codes = dev_alloc<uint32_t>(kCap, "codes");
+    c->d_info = dev_alloc<uint32_t>(4, "info");
+    c->d_misc = dev_alloc<float>(192 + 1280 + 1024 + 2 * 8448, "misc buffers");
+    ck(cudaMallocHost(&c->h_stage, T * kW * 4), "pinned staging");
+    ck(cudaMallocHost(&c->h_logits, size_t(kVocab) * 10 * 4), "pinned logits");
+    ck(cudaMallocHost(&c->h_codes, kCap * 4), "pinned codes");
+    ck(cudaMallocHost(&c->h_ctl, sizeof(itts::DecodeCtl)), "pinned control");
+    c->d_model = dev_alloc<itts::ModelW>(1, "model table");
+    ck(cudaMemcpy(c->d_model, &c->hw, sizeof(itts::ModelW), cudaMemcpyHostToDevice), "model table upload");
+}
+
+// ------------------------------------------------------------- execution
+void check_status(itts_gpt_ctx* c) {
+    ck(cudaMemcpyAsync(c->h_ctl, c->db.ctl, sizeof(itts::DecodeCtl), cudaMemcpyDeviceToHost, c->stream), "status read");
+    ck(cudaStreamSynchronize(c->stream), "stream sync");
+    const int code = c->h_ctl->status[0];
+    if (!code) return;
+    const std::string where = " (site " + std::to_string(c->h_ctl->status[1]) + ", cta " +
+                              std::to_string(c->h_ctl->status[2]) + ", detail " + std::to_string(c->h_ctl->status[3]) + ")";
+    switch (code) {
+        case itts::kStatusInvalidCode: fail(ITTS_ERR_RUNTIME, "GPT generated invalid semantic code");
+        case itts::kStatusNoFiniteLogits: fail(ITTS_ERR_RUNTIME, "GPT sampling received no finite logits");
+        case itts::kStatusZeroMass: fail(ITTS_ERR_RUNTIME, "GPT sampling probability mass is zero");
+        case itts::kStatusBarrierTimeout: fail(ITTS_ERR_DEVICE_TIMEOUT, "device grid barrier timed out" + where);
+        default: fail(ITTS_ERR_RUNTIME, "device error " + std::to_string(code) + where);
+    }
+}
+
+void finish_pending(itts_gpt_ctx* c) {
+    if (!c->pending) return;
+    c->pending = false;
+    uint32_t info[4] = {0, 0, 0, 0};
+    ck(cudaMemcpyAsync(info, c->pending_info, sizeof info, cudaMemcpyDeviceToHost, c->stream), "info read");
+    check_status(c);
+    c->cached += info[3];
+}
+
+void reset_ctl(itts_gpt_ctx* c) {
+    ck(cudaMemsetAsync(c->db.ctl, 0, sizeof(itts::DecodeCtl), c->stream), "control reset");
+}
+
+itts::DecodeArgs decode_args(itts_gpt_ctx* c) {
+    itts::DecodeArgs a{};
+    a.w = c->d_model;
+    a.b = c->db;
+    a.history = c->d_history;
+    a.history_n = 2;
+    a.codes = c->d_codes;
+    return a;
+}
+
+void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
+    reset_ctl(c);
+    if (c->mode == 0) {
+        ck(itts::launch_decode_persistent(a, c->sm_count, c->stream), "persistent decode launch");
+        ++c->launches;
+    } else {
+        ck(itts::launch_decode_layered(a, int(c->layers), c->sm_count, c->stream, &c->launches), "layered decode launch");
+    }
+}
+
+// prefix already in d_hidden
+void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
+    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x, c->d_qkv, c->d_att, c->d_r, c->d_ff, c->d_kv, int(rows)};
+    ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
+    ck(cudaMemcpyAsync(c->db.h, c->d_hidden + size_t(rows - 1) * kW, kW * 4, cudaMemcpyDeviceToDevice, c->stream),
+       "last row copy");
+    reset_ctl(c);
+    ck(itts::launch_head(decode_args(c), c->sm_count, c->stream), "head launch");
+    ++c->launches;
+}
+
+void validate_prefix(size_t n_floats) {
+    if (n_floats == 0 || n_floats % kW || n_floats / kW > 1024) invalid("Invalid GPT prefill dimensions");
+}
+
+void host_prefill(itts_gpt_ctx* c, const float* prefix, size_t n_floats) {
+    validate_prefix(n_floats);
+    if (!prefix) invalid("prefix is null");
+    const uint32_t rows = uint32_t(n_floats / kW);
+    std::memcpy(c->h_stage, prefix, n_floats * 4);
+    ck(cudaMemcpyAsync(c->d_hidden, c->h_stage, n_floats * 4, cudaMemcpyHostToDevice, c->stream), "prefix upload");
+    run_prefill(c, rows);
+    c->cached = rows;
+    c->prefix_rows = rows;
+    c->have_prefill = true;
+}
+
+// gpt_sampling.cpp:170-173
+itts::SampleOpts configure(const itts_gen_opts& in, float* length_penalty) {
+    itts_gen_opts o = in;
+    if (!o.do_sample) {
+        o.temperature = 1;
+        o.top_k = 0;
+        o.top_p = 1;
+    }
+    if (!std::isfinite(o.temperature) || !std::isfinite(o.top_p) || !std::isfinite(o.repetition_penalty) ||
+        o.temperature <= 0 || o.top_p <= 0 || o.top_p > 1 || o.repetition_penalty <= 0)
+        invalid("Invalid GPT generation parameters");
+    if (!o.num_beams || o.num_beams > 10 || !std::isfinite(o.length_penalty))
+        invalid("Invalid beam search configuration");
+    if (o.rng != ITTS_RNG_SPLITMIX64 && o.rng != ITTS_RNG_PHILOX) invalid("Invalid random stream selector");
+    if (length_penalty) *length_penalty = o.length_penalty;
+    return itts::SampleOpts{o.do_sample, o.top_k, o.seed, o.temperature, o.top_p, o.repetition_penalty, o.num_beams,
+                            o.rng};
+}
+
+void validate_capacity(itts_gpt_ctx* c, size_t prefix_rows, uint32_t maximum) {
+    if (!maximum || maximum + 1 >= c->mel_pos_rows || prefix_rows + maximum >= kCap)
+        invalid("GPT generation capacity exceeded");
+}
+
+// one cached decode step with `code` at `pos`; logits stay in db.logits
+void device_step(itts_gpt_ctx* c, uint32_t code, uint32_t pos) {
+    if (!c->cached || c->cached >= kCap || code >= kVocab || pos >= c->mel_pos_rows)
+        invalid("GPT step requires valid cache, code and position");
+    itts::DecodeArgs a = decode_args(c);
+    a.mode = itts::kModeStep;
+    a.n_iter = 1;
+    a.s0 = c->cached;
+    a.pos0 = pos;
+    a.first_code = code;
+    launch_decode(c, a);
+    ++c->cached;
+}
+
+// ------------------------------------------------------------ KV states
+itts_gpt_state* make_checkpoint(itts_gpt_ctx* c) {
+    if (!c->cached) invalid("Invalid KV snapshot");
+    auto s = std::make_unique<itts_gpt_state>();
+    s->device = c->device;
+    s->tokens = c->cached;
+    s->layers = c->layers;
+    s->d = dev_alloc<float>(size_t(c->layers) * 2 * kH * c->cached * kHd, "KV snapshot");
+    const size_t width = size_t(c->cached) * kHd * 4;
+    for (uint32_t l = 0; l < c->layers * 2; ++l)
+        ck(cudaMemcpy2DAsync(s->d + size_t(l) * kH * c->cached * kHd, width,
+                             c->d_kv + size_t(l) * kH * kCap * kHd, size_t(kCap) * kHd * 4, width, kH,
+                             cudaMemcpyDeviceToDevice, c->stream),
+           "KV snapshot copy");
+    return s.release();
+}
+
+void apply_restore(itts_gpt_ctx* c, const itts_gpt_state* s) {
+    if (!s || s->layers != c->layers || s->device != c->device || !s->tokens || s->tokens > kCap)
+        invalid("Invalid KV restore");
+    const size_t width = size_t(s->tokens) * kHd * 4;
+    for (uint32_t l = 0; l < c->layers * 2; ++l)
+        ck(cudaMemcpy2DAsync(c->d_kv + size_t(l) * kH * kCap * kHd, size_t(kCap) * kHd * 4,
+                             s->d + size_t(l) * kH * s->tokens * kHd, width, width, kH, cudaMemcpyDeviceToDevice,
+                             c->stream),
+           "KV restore copy");
+    c->cached = s->tokens;
+}
+
+// ------------------------------------------------------------ beam search
+// gpt_sampling.cpp:190-245.  The per-parent log-softmax, processors and beam
+// score run on the device (launch_beam_scores); candidate selection and the
+// hypothesis bookkeeping are the reference's host logic.
+uint64_t splitmix_draw(uint64_t seed, uint64_t n) {
+    uint64_t z = seed + (n + 1) * 0x9E3779B97F4A7C15ULL;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+uint64_t philox_draw(uint64_t seed, uint64_t draw) {
+    uint32_t c0 = uint32_t(draw), c1 = uint32_t(draw >> 32), c2 = 0, c3 = 0;
+    uint32_t k0 = uint32_t(seed), k1 = uint32_t(seed >> 32);
+    for (int r = 0; r < 10; ++r) {
+        const uint64_t p0 = uint64_t(0xD2511F53u) * c0, p1 = uint64_t(0xCD9E8D57u) * c2;
+        const uint32_t n0 = uint32_t(p1 >> 32) ^ c1 ^ k0, n1 = uint32_t(p1), n2 = uint32_t(p0 >> 32) ^ c3 ^ k1,
+                       n3 = uint32_t(p0);
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return (uint64_t(c0) << 32) | c1;
+}
+
+// sample_gpt_token_from_logits (gpt_sampling.cpp:130-165) over n*8194 scores.
+uint32_t sample_flat(const std::vector<float>& s, int rng, uint64_t seed, uint64_t draw) {
+    float mx = -std::numeric_limits<float>::infinity();
+    for (float v : s)
+        if (std::isfinite(v)) mx = std::max(mx, v);
+    if (!std::isfinite(mx)) fail(ITTS_ERR_RUNTIME, "GPT sampling received no finite logits");
+    double total = 0.0;
+    std::vector<double> probs(s.size(), 0.0);
+    for (size_t i = 0; i < s.size(); ++i)
+        if (std::isfinite(s[i])) {
+            probs[i] = std::exp(static_cast<double>(s[i] - mx));
+            total += probs[i];
+        }
+    if (total <= 0.0) fail(ITTS_ERR_RUNTIME, "GPT sampling probability mass is zero");
+    const uint64_t u = rng == 1 ? philox_draw(seed, draw) : splitmix_draw(seed, draw);
+    const double target = static_cast<double>(u >> 11) * (1.0 / 9007199254740992.0) * total;
+    double cum = 0.0;
+    uint32_t last = 0;
+    for (uint32_t i = 0; i < probs.size(); ++i) {
+        if (probs[i] <= 0.0) continue;
+        last = i;
+        cum += probs[i];
+        if (target < cum) return i;
+    }
+    return last;
+}
+
+std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n_floats, const itts::SampleOpts& o,
+                                  float length_penalty, uint32_t maximum, bool& eos_out) {
+    const uint32_t nb = o.num_beams;
+    // slots: 2 * nb logits buffers + scratch + nb * 8194 scores
+    const uint32_t need = (2 * nb + 1 + nb) * 8448;
+    if (c->beam_cap < need) {
+        if (c->d_beam) cudaFree(c->d_beam);
+        c->d_beam = nullptr;
+        c->d_beam = dev_alloc<float>(need, "beam buffers");
+        c->beam_cap = need;
+    }
+    float* slots = c->d_beam;
+    float* tmp = slots + size_t(2 * nb) * 8448;
+    float* scores = tmp + 8448;
+    struct Beam {
+        std::vector<uint32_t> codes;
+        float score = 0;
+        int slot = -1;
+        std::shared_ptr<itts_gpt_state> state;
+    };
+    struct Finished {
+        std::vector<uint32_t> codes;
+        double score;
+        bool eos;
+    };
+    struct Cand {
+        uint32_t parent, token;
+        float score;
+    };
+    uint64_t draws = 0;
+    std::vector<Finished> finished;
+    host_prefill(c, prefix, n_floats);
+    ck(cudaMemcpyAsync(slots, c->db.logits, kVocab * 4, cudaMemcpyDeviceToDevice, c->stream), "beam logits");
+    Beam init;
+    init.slot = 0;
+    init.state.reset(make_checkpoint(c));
+    std::vector<Beam> beams(nb, init);
+    for (uint32_t i = 1; i < beams.size(); ++i) beams[i].score = -1e9f;
+    auto finish = [&](const Beam& beam, float score, uint32_t length, bool eos) {
+        finished.push_back({beam.codes, score / std::pow(static_cast<double>(std::max(length, 1u)), length_penalty), eos});
+        std::sort(finished.begin(), finished.end(), [](const Finished& a, const Finished& b) { return a.score > b.score; });
+        if (finished.size() > nb) finished.resize(nb);
+    };
+    std::vector<uint32_t> hist;
+    std::vector<float> all;
+    for (uint32_t si = 0; si < maximum; ++si) {
+        reset_ctl(c);
+        for (uint32_t p = 0; p < beams.size(); ++p) {
+            hist.assign({1u, 8192u});
+            hist.insert(hist.end(), beams[p].codes.begin(), beams[p].codes.end());
+            if (c->d_hist_cap < hist.size()) {
+                if (c->d_hist) cudaFree(c->d_hist);
+                c->d_hist = nullptr;
+                c->d_hist_cap = std::max<size_t>(hist.size(), 4096);
+                c->d_hist = dev_alloc<uint32_t>(c->d_hist_cap * (nb + 1), "history buffer");
+            }
+            uint32_t* dh = c->d_hist + size_t(p) * c->d_hist_cap;
+            ck(cudaMemcpyAsync(dh, hist.data(), hist.size() * 4, cudaMemcpyHostToDevice, c->stream), "history upload");
+            ck(itts::launch_beam_scores(slots + size_t(beams[p].slot) * 8448, o, dh, uint32_t(hist.size()),
+                                        beams[p].score, tmp, scores + size_t(p) * kVocab, c->db.ctl->status, c->stream),
+               "beam score launch");
+            ++c->launches;
+            ck(cudaStreamSynchronize(c->stream), "beam score");  // hist staging is reused per parent
+        }
+        all.resize(size_t(beams.size()) * kVocab);
+        ck(cudaMemcpyAsync(all.data(), scores, all.size() * 4, cudaMemcpyDeviceToHost, c->stream), "beam scores read");
+        check_status(c);
+        std::vector<Cand> cands;
+        const uint32_t take = 2 * nb;
+        if (o.do_sample) {
+            auto avail = all;
+            for (uint32_t i = 0; i < take; ++i) {
+                const uint32_t id = sample_flat(avail, o.rng, o.seed, draws++);
+                cands.push_back({id / kVocab, id % kVocab, all[id]});
+                avail[id] = -std::numeric_limits<float>::infinity();
+            }
+        } else {
+            std::vector<uint32_t> order(all.size());
+            std::iota(order.begin(), order.end(), 0u);
+            std::partial_sort(order.begin(), order.begin() + take, order.end(), [&](uint32_t a, uint32_t b) {
+                return all[a] == all[b] ? a < b : all[a] > all[b];
+            });
+            for (uint32_t i = 0; i < take; ++i) cands.push_back({order[i] / kVocab, order[i] % kVocab, all[order[i]]});
+        }
+        std::sort(cands.begin(), cands.end(), [](const Cand& a, const Cand& b) { return a.score > b.score; });
+        std::vector<Beam> next;
+        const int slot_base = int((si + 1) % 2) * int(nb);
+        for (uint32_t rank = 0; rank < cands.size(); ++rank) {
+            const Cand cand = cands[rank];
+            const Beam& parent = beams[cand.parent];
+            if (cand.token == 8193) {
+                if (rank < nb) finish(parent, cand.score, si + 1, true);
+                continue;
+            }
+            if (cand.token >= 8192) fail(ITTS_ERR_RUNTIME, "Beam generated invalid semantic code");
+            Beam child;
+            child.codes = parent.codes;
+            child.codes.push_back(cand.token);
+            child.score = cand.score;
+            if (si + 1 < maximum) {
+                apply_restore(c, parent.state.get());
+                device_step(c, cand.token, si + 2);
+                child.slot = slot_base + int(next.size());
+                ck(cudaMemcpyAsync(slots + size_t(child.slot) * 8448, c->db.logits, kVocab * 4,
+                                   cudaMemcpyDeviceToDevice, c->stream),
+                   "beam logits");
+                child.state.reset(make_checkpoint(c));
+            }
+            next.push_back(std::move(child));
+            if (next.size() == nb) break;
+        }
+        if (next.empty()) break;
+        beams = std::move(next);
+        if (finished.size() == nb &&
+            finished.back().score >= cands[0].score / std::pow(static_cast<double>(si + 1), length_penalty)) {
+            beams.clear();
+            break;
+        }
+    }
+    check_status(c);
+    for (const auto& beam : beams) finish(beam, beam.score, uint32_t(beam.codes.size()), false);
+    if (finished.empty()) fail(ITTS_ERR_RUNTIME, "Beam search produced no hypotheses");
+    eos_out = finished[0].eos;
+    return finished[0].codes;
+}
+
+}  // namespace
+
+// ================================================================ C-ABI
+extern "C" {
+
+void itts_gen_opts_default(itts_gen_opts* o) {
+    if (!o) return;
+    o->do_sample = 1;
+    o->top_k = 30;
+    o->seed = 20261002ull;
+    o->temperature = 0.8f;
+    o->top_p = 0.8f;
+    o->repetition_penalty = 10.0f;
+    o->num_beams = 1;
+    o->length_penalty = 0.0f;
+    o->rng = ITTS_RNG_SPLITMIX64;
+}
+
+const char* itts_gpt_last_error(const itts_gpt_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_error.c_str(); }
+
+int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_gpt_ctx** out) {
+    g_create_error.clear();
+    if (!out) {
+        g_create_error = "out is null";
+        return ITTS_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    std::unique_ptr<itts_gpt_ctx> c(new (std::nothrow) itts_gpt_ctx());
+    if (!c) return ITTS_ERR_OUT_OF_MEMORY;
+    c->device = device;
+    c->dtype = weight_dtype;
+    const int rc = guard(c.get(), [&] {
+        if (!bundle_dir) invalid("bundle_dir is null");
+        if (weight_dtype != ITTS_WEIGHTS_F32)
+            invalid("weight_dtype: only ITTS_WEIGHTS_F32 is available in this build");
+        itts::Mit2Bundle bundle(bundle_dir);
+        validate_bundle(c.get(), bundle);
+        int n = 0;
+        ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (device < 0 || device >= n) invalid("device index out of range");
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        cudaDeviceProp prop{};
+        ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major < 10) fail(ITTS_ERR_RUNTIME, "this library is built for sm_100a (B200) devices only");
+        c->sm_count = prop.multiProcessorCount;
+        if (!prop.cooperativeLaunch) fail(ITTS_ERR_RUNTIME, "device lacks cooperative launch");
+        int per_sm = 0;
+        ck(itts::decode_configure(&per_sm), "decode kernel configuration");
+        if (per_sm < 1) fail(ITTS_ERR_RUNTIME, "persistent decode kernel does not fit on an SM");
+        ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream creation");
+        upload_weights(c.get(), bundle);
+        alloc_buffers(c.get());
+        ck(cudaDeviceSynchronize(), "load");
+    }, /*set_device=*/false);
+    if (rc != ITTS_OK) {
+        g_create_error = c->err;
+        return rc;
+    }
+    *out = c.release();
+    return ITTS_OK;
+}
+
+void itts_gpt_destroy(itts_gpt_ctx* ctx) { delete ctx; }
+
+int itts_gpt_get_info(const itts_gpt_ctx* ctx, itts_gpt_info* info) {
+    if (!ctx || !info) return ITTS_ERR_INVALID_ARGUMENT;
+    info->layers = ctx->layers;
+    info->mel_pos_rows = ctx->mel_pos_rows;
+    info->text_pos_rows = ctx->text_pos_rows;
+    info->sm_count = uint32_t(ctx->sm_count);
+    info->weight_bytes = ctx->weight_bytes;
+    info->stream_bytes = ctx->stream_bytes;
+    info->weight_dtype = ctx->dtype;
+    info->device = ctx->device;
+    return ITTS_OK;
+}
+
+int itts_gpt_prepare(itts_gpt_ctx* ctx, const float* speaker, size_t speaker_n, const float* emotion, size_t emotion_n,
+                     const uint32_t* text, size_t text_n, uint32_t language, float* out, size_t out_floats,
+                     size_t* rows) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (speaker_n != 192 || emotion_n != kW || language >= 107 || !speaker || !emotion)
+            invalid("Invalid GPT conditioning dimensions");
+        std::vector<uint32_t> ids{0};
+        for (size_t i = 0; i < text_n; ++i) {
+            const uint32_t id = text[i];
+            if (id >= 60510) invalid("Text token is outside 2.5 vocabulary");
+            if (id != 0 && id != 1) ids.push_back(id);
+        }
+        ids.push_back(1);
+        if (ids.size() > 602 || ids.size() > ctx->text_pos_rows) invalid("Text segment exceeds GPT position capacity");
+        const size_t nrows = 3 + ids.size() + 1;
+        if (!out || !rows || out_floats < nrows * kW) invalid("output buffer too small");
+        float* d_spk = ctx->d_misc;
+        float* d_emo = d_spk + 192;
+        uint32_t* d_ids = reinterpret_cast<uint32_t*>(d_emo + 1280);
+        ck(cudaMemcpyAsync(d_spk, speaker, 192 * 4, cudaMemcpyHostToDevice, ctx->stream), "speaker upload");
+        ck(cudaMemcpyAsync(d_emo, emotion, kW * 4, cudaMemcpyHostToDevice, ctx->stream), "emotion upload");
+        ck(cudaMemcpyAsync(d_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, ctx->stream), "ids upload");
+        itts::PrepareArgs a{ctx->spk_w, ctx->spk_b, ctx->text_emb, ctx->text_pos, ctx->lang_emb, ctx->hw.mel_emb,
+                            ctx->hw.mel_pos, d_spk, d_emo, d_ids, uint32_t(ids.size()), language, ctx->d_x};
+        ck(itts::launch_prepare(a, ctx->stream), "prepare launch");
+        ++ctx->launches;
+        ck(cudaMemcpyAsync(ctx->h_stage, ctx->d_x, nrows * kW * 4, cudaMemcpyDeviceToHost, ctx->stream), "prefix read");
+        ck(cudaStreamSynchronize(ctx->stream), "prepare");
+        std::memcpy(out, ctx->h_stage, nrows * kW * 4);
+        *rows = nrows;
+    });
+}
+
+int itts_gpt_prefill(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, float* logits) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        host_prefill(ctx, prefix, n_floats);
+        if (logits) ck(cudaMemcpyAsync(ctx->h_logits, ctx->db.logits, kVocab * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "logits read");
+        check_status(ctx);
+        if (logits) std::memcpy(logits, ctx->h_logits, kVocab * 4);
+    });
+}
+
+int itts_gpt_step(itts_gpt_ctx* ctx, uint32_t code, uint32_t position, float* logits) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        device_step(ctx, code, position);
+        if (logits) ck(cudaMemcpyAsync(ctx->h_logits, ctx->db.logits, kVocab * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "logits read");
+        check_status(ctx);
+        if (logits) std::memcpy(logits, ctx->h_logits, kVocab * 4);
+    });
+}
+
+int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const itts_gen_opts* opts,
+                      uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes, int* stopped) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (!opts || !codes || !n_codes || !stopped) invalid("null output or options");
+        validate_capacity(ctx, n_floats / kW, max_tokens);
+        float lp = 0;
+        const itts::SampleOpts o = configure(*opts, &lp);
+        if (o.num_beams > 1) {
+            bool eos = false;
+            auto r = beam_search(ctx, prefix, n_floats, o, lp, max_tokens, eos);
+            std::memcpy(codes, r.data(), r.size() * 4);
+            *n_codes = uint32_t(r.size());
+            *stopped = eos ? 1 : 0;
+            return;
+        }
+        host_prefill(ctx, prefix, n_floats);
+        itts::DecodeArgs a = decode_args(ctx);
+        a.mode = itts::kModeGenerate;
+        a.n_iter = max_tokens;
+        a.s0 = ctx->cached;
+        a.pos0 = 2;  // first generated code sits at mel position 2 (gpt_sampling.cpp:184-186)
+        a.opts = o;
+        launch_decode(ctx, a);
+        ck(cudaMemcpyAsync(ctx->h_codes, ctx->d_codes, size_t(max_tokens) * 4, cudaMemcpyDeviceToHost, ctx->stream),
+           "codes read");
+        check_status(ctx);
+        const itts::DecodeCtl& ctl = *ctx->h_ctl;
+        ctx->cached += ctl.info[3];
+        *n_codes = ctl.info[0];
+        *stopped = int(ctl.info[1]);
+        std::memcpy(codes, ctx->h_codes, size_t(ctl.info[0]) * 4);
+    });
+}
+
+int itts_gpt_checkpoint(itts_gpt_ctx* ctx, itts_gpt_state** out) {
+    if (!ctx || !out) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        *out = make_checkpoint(ctx);
+        ck(cudaStreamSynchronize(ctx->stream), "snapshot");
+    });
+}
+
+int itts_gpt_restore(itts_gpt_ctx* ctx, const itts_gpt_state* state) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        apply_restore(ctx, state);
+        ck(cudaStreamSynchronize(ctx->stream), "restore");
+    });
+}
+
+void itts_gpt_state_free(itts_gpt_state* state) { delete state; }
+
+uint32_t itts_gpt_cached_tokens(const itts_gpt_ctx* ctx) { return ctx ? ctx->cached : 0; }
+
+int itts_gpt_apply_processors(itts_gpt_ctx* ctx, const float* logits, size_t n, const uint32_t* history,
+                              size_t history_n, const itts_gen_opts* opts, float* out) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (!logits || !out || !opts || (history_n && !history)) invalid("null argument");
+        if (n != kVocab) invalid("logits must have 8194 entries");
+        // gpt_sampling.cpp:33-71 error checks
+        if (opts->repetition_penalty != 1.0f && opts->repetition_penalty <= 0.0f)
+            fail(ITTS_ERR_RUNTIME, "GPT repetition penalty must be positive");
+        if (opts->temperature <= 0.0f) fail(ITTS_ERR_RUNTIME, "GPT sampling temperature must be positive");
+        if (opts->top_p < 1.0f && opts->top_p <= 0.0f) fail(ITTS_ERR_RUNTIME, "GPT top_p must be in (0, 1]");
+        if (ctx->d_hist_cap < std::max<size_t>(history_n, 1)) {
+            if (ctx->d_hist) cudaFree(ctx->d_hist);
+            ctx->d_hist = nullptr;
+            ctx->d_hist_cap = std::max<size_t>(history_n, 4096);
+            ctx->d_hist = dev_alloc<uint32_t>(ctx->d_hist_cap * 11, "history buffer");
+        }
+        float* d_in = ctx->d_misc + 192 + 1280 + 1024;
+        float* d_out = d_in + 8448;
+        std::memcpy(ctx->h_logits, logits, kVocab * 4);
+        ck(cudaMemcpyAsync(d_in, ctx->h_logits, kVocab * 4, cudaMemcpyHostToDevice, ctx->stream), "logits upload");
+        if (history_n)
+            ck(cudaMemcpyAsync(ctx->d_hist, history, history_n * 4, cudaMemcpyHostToDevice, ctx->stream),
+               "history upload");
+        const itts::SampleOpts o{opts->do_sample, opts->top_k, opts->seed, opts->temperature, opts->top_p,
+                                 opts->repetition_penalty, opts->num_beams, opts->rng};
+        reset_ctl(ctx);
+        ck(itts::launch_processors(d_in, o, ctx->d_hist, uint32_t(history_n), d_out, ctx->db.ctl->status, ctx->stream),
+           "processors launch");
+        ++ctx->launches;
+        ck(cudaMemcpyAsync(ctx->h_logits + 8448, d_out, kVocab * 4, cudaMemcpyDeviceToHost, ctx->stream), "scores read");
+        check_status(ctx);
+        std::memcpy(out, ctx->h_logits + 8448, kVocab * 4);
+    });
+}
+
+int itts_gpt_stream(itts_gpt_ctx* ctx, void** cuda_stream) {
+    if (!ctx || !cuda_stream) return ITTS_ERR_INVALID_ARGUMENT;
+    *cuda_stream = ctx->stream;
+    return ITTS_OK;
+}
+
+int itts_gpt_prefill_async(itts_gpt_ctx* ctx, const float* d_prefix, uint32_t rows, float* d_logits) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        validate_prefix(size_t(rows) * kW);
+        if (!d_prefix) invalid("prefix is null");
+        ck(cudaMemcpyAsync(ctx->d_hidden, d_prefix, size_t(rows) * kW * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+           "prefix copy");
+        run_prefill(ctx, rows);
+        if (d_logits)
+            ck(cudaMemcpyAsync(d_logits, ctx->db.logits, kVocab * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+               "logits copy");
+        ctx->cached = rows;
+        ctx->prefix_rows = rows;
+        ctx->have_prefill = true;
+    });
+}
+
+int itts_gpt_decode_async(itts_gpt_ctx* ctx, const itts_gen_opts* opts, uint32_t max_tokens, uint32_t* d_codes,
+                          uint32_t* d_info) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (!opts || !d_codes || !d_info) invalid("null output or options");
+        if (!ctx->have_prefill || ctx->cached != ctx->prefix_rows)
+            fail(ITTS_ERR_LOGIC, "decode_async must directly follow a prefill");
+        validate_capacity(ctx, ctx->prefix_rows, max_tokens);
+        const itts::SampleOpts o = configure(*opts, nullptr);
+        if (o.num_beams > 1) invalid("decode_async supports num_beams == 1");
+        itts::DecodeArgs a = decode_args(ctx);
+        a.mode = itts::kModeGenerate;
+        a.n_iter = max_tokens;
+        a.s0 = ctx->cached;
+        a.pos0 = 2;
+        a.opts = o;
+        a.codes = d_codes;
+        a.info_out = d_info;
+        launch_decode(ctx, a);
+        ctx->have_prefill = false;
+        ctx->pending = true;
+        ctx->pending_info = d_info;
+    });
+}
+
+int itts_gpt_sync(itts_gpt_ctx* ctx) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        if (ctx->pending)
+            finish_pending(ctx);
+        else
+            check_status(ctx);
+    });
+}
+
+int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode) {
+    if (!ctx || (mode != 0 && mode != 1)) return ITTS_ERR_INVALID_ARGUMENT;
+    ctx->mode = mode;
+    return ITTS_OK;
+}
+
+uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+// Device-side model description and kernel arguments of the B200 GPT decoder.
+// Plain structs shared by the host runtime (itts_gpt.cpp) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace itts {
+
+// Device status word (int32[4]): {code, where, cta, detail}.  Written once by
+// the first failing CTA (atomicCAS on code) and read by the host after a sync.
+enum DeviceStatus : int {
+    kStatusOk = 0,
+    kStatusBarrierTimeout = 1,   // a grid barrier wait exceeded its time limit
+    kStatusInvalidCode = 2,      // sampled code 8192 (gpt_sampling.cpp:182)
+    kStatusNoFiniteLogits = 3,   // sampling/top-p saw no finite score
+    kStatusZeroMass = 4,         // probability mass was zero
+};
+
+
+// One transformer block.  Matrices are row-major [out, in] fp32 (the Conv1D
+// [in, out] tensors of the bundle are transposed once on the device at load,
+// the transpose the reference caches on the CPU in gpt.cpp:24-33).
+struct LayerW {
+    const float *ln1_g, *ln1_b;
+    const float *w_qkv, *b_qkv;  // [3840, 1280]
+    const float *w_o, *b_o;      // [1280, 1280]
+    const float *ln2_g, *ln2_b;
+    const float *w_fc, *b_fc;    // [5120, 1280]
+    const float *w_mp, *b_mp;    // [1280, 5120]
+};
+
+struct ModelW {
+    LayerW layer[24];
+    int layers;
+    const float *lnf_g, *lnf_b;  // gpt.gpt.ln_f
+    const float *fn_g, *fn_b;    // gpt.final_norm
+    const float *w_head, *b_head;  // gpt.mel_head [8194, 1280] (nn.Linear layout)
+    const float *mel_emb, *mel_pos;
+};
+
+// Sampling options after GenerationOptions validation (gpt_sampling.cpp:168-173).
+struct SampleOpts {
+    int do_sample;
+    uint32_t top_k;
+    uint64_t seed;
+    float temperature;
+    float top_p;
+    float rp;  // repetition penalty
+    uint32_t num_beams;
+    int rng;   // 0 SplitMix64, 1 Philox4x32-10
+};
+
+// Small control block, zeroed before every decode launch.
+struct DecodeCtl {
+    int status[4];       // {code, where, cta, detail}
+    uint32_t info[4];    // {n_codes, stopped, status, forward_steps}
+    unsigned bar;        // grid-barrier arrival counter (monotonic per launch)
+    unsigned head_cnt[20];  // split-K attention arrival counters per head
+    uint32_t token;      // current code (layered mode)
+    int done;            // layered mode: loop finished
+    unsigned pad[5];
+};
+
+// Decode-time device buffers (activations live in L2; KV cache in HBM).
+struct DecodeBuffers {
+    float* kv;        // [layer][K|V][head][4096][64] fp32
+    float* h;         // residual stream [1280]
+    float* qkv;       // [3840]
+    float* attn;      // [1280]
+    float* r;         // [1280]
+    float* ff;        // [5120]
+    float* logits;    // [8194]
+    float* part;      // split-K partials [20 * 512 * 66]
+    DecodeCtl* ctl;
+};
+
+enum DecodeMode : int { kModeStep = 0, kModeGenerate = 1 };
+
+struct DecodeArgs {
+    const ModelW* w;  // device copy
+    DecodeBuffers b;
+    int mode;
+    uint32_t n_iter;      // kModeStep: 1; kModeGenerate: max_tokens
+    uint32_t s0;          // cached tokens before the first forward step
+    uint32_t pos0;        // mel position of the first forward step
+    uint32_t first_code;  // kModeStep: the input code
+    SampleOpts opts;
+    const uint32_t* history;  // initial repetition-penalty history ({1, 8192})
+    uint32_t history_n;
+    uint32_t* codes;      // kModeGenerate output [n_iter]
+    uint32_t* info_out;   // optional copy of ctl->info (may be null)
+};
+
+// ---- host-side launchers (decode.cu, prefill.cu, misc.cu) -----------------
+size_t decode_smem_bytes();
+cudaError_t decode_configure(int* blocks_per_sm);
+cudaError_t launch_decode_persistent(const DecodeArgs& a, int ncta, cudaStream_t s);
+cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cudaStream_t s, uint64_t* launches);
+cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s);
+cudaError_t launch_processors(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
+                              float* out, int* status, cudaStream_t s);
+
+struct PrefillArgs {
+    const ModelW* hw;  // host copy (pointers to device memory)
+    float* hidden;     // [T, 1280] in: prefix, out: last hidden state
+    float* x;          // [T, 1280]
+    float* qkv;        // [T, 3840]
+    float* att;        // [T, 1280]
+    float* r;          // [T, 1280]
+    float* ff;         // [T, 5120]
+    float* kv;
+    int T;
+};
+cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
+
+cudaError_t launch_transpose(const float* in, float* out, int rows_in, int cols_in, cudaStream_t s);
+struct PrepareArgs {
+    const float *spk_w, *spk_b, *text_emb, *text_pos, *lang_emb, *mel_emb, *mel_pos;
+    const float *speaker, *emotion;
+    const uint32_t* ids;
+    uint32_t n_ids, language;
+    float* out;  // [(3 + n_ids + 1), 1280]
+};
+cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t s);
+
+}  // namespace itts

@@ -53,9 +53,8 @@ struct SplitMix64 {
 // Philox4x32 with 10 rounds (Salmon, Moraes, Dror, Shaw, "Parallel random
 // numbers: as easy as 1, 2, 3", SC'11): counter = (draw_lo, draw_hi, 0, 0),
 // key = (seed_lo, seed_hi); the first two output words form the 64-bit draw.
-inline uint64_t philox_u64(uint64_t seed, uint64_t draw) {
-    uint32_t c0 = uint32_t(draw), c1 = uint32_t(draw >> 32), c2 = 0, c3 = 0;
-    uint32_t k0 = uint32_t(seed), k1 = uint32_t(seed >> 32);
+inline void philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3], k0 = key[0], k1 = key[1];
     for (int r = 0; r < 10; ++r) {
         const uint64_t p0 = uint64_t(0xD2511F53u) * c0, p1 = uint64_t(0xCD9E8D57u) * c2;
         const uint32_t n0 = uint32_t(p1 >> 32) ^ c1 ^ k0, n1 = uint32_t(p1);
@@ -64,7 +63,14 @@ inline uint64_t philox_u64(uint64_t seed, uint64_t draw) {
         k0 += 0x9E3779B9u;
         k1 += 0xBB67AE85u;
     }
-    return (uint64_t(c0) << 32) | c1;
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+inline uint64_t philox_u64(uint64_t seed, uint64_t draw) {
+    const uint32_t ctr[4] = {uint32_t(draw), uint32_t(draw >> 32), 0, 0}, key[2] = {uint32_t(seed), uint32_t(seed >> 32)};
+    uint32_t o[4];
+    philox4x32_10(ctr, key, o);
+    return (uint64_t(o[0]) << 32) | o[1];
 }
 
 struct Uniform {
@@ -551,6 +557,14 @@ int orc_sample(const float* scores, size_t n, int rng, uint64_t seed, uint64_t d
         for (uint64_t i = 0; i < draw; ++i) u.next();
         *token = orc::sample_token(std::vector<float>(scores, scores + n), u);
     });
+}
+
+void orc_philox4x32_10(const uint32_t* ctr, const uint32_t* key, uint32_t* out) { orc::philox4x32_10(ctr, key, out); }
+
+uint64_t orc_splitmix64(uint64_t seed, uint64_t draw) {
+    orc::SplitMix64 s(seed);
+    for (uint64_t i = 0; i < draw; ++i) s.next_u64();
+    return s.next_u64();
 }
 
 double orc_uniform(int rng, uint64_t seed, uint64_t draw) {

@@ -93,6 +93,9 @@ class _Oracle:
                                                 C.POINTER(C.c_uint32)]
                 cls._lib.orc_uniform.restype = C.c_double
                 cls._lib.orc_uniform.argtypes = [C.c_int, C.c_uint64, C.c_uint64]
+                cls._lib.orc_philox4x32_10.argtypes = [C.POINTER(C.c_uint32)] * 3
+                cls._lib.orc_splitmix64.restype = C.c_uint64
+                cls._lib.orc_splitmix64.argtypes = [C.c_uint64, C.c_uint64]
                 cls._lib.orc_layers.restype = C.c_uint32
                 cls._lib.orc_layers.argtypes = [C.c_void_p]
         return cls._lib
@@ -198,6 +201,18 @@ class PortOracle(_Oracle):
         if rc != 0:
             raise OracleError(rc, cls.lib().orc_last_error().decode())
         return tok.value
+
+    @classmethod
+    def philox4x32_10(cls, ctr, key):
+        c = (C.c_uint32 * 4)(*ctr)
+        k = (C.c_uint32 * 2)(*key)
+        o = (C.c_uint32 * 4)()
+        cls.lib().orc_philox4x32_10(c, k, o)
+        return list(o)
+
+    @classmethod
+    def splitmix64(cls, seed: int, draw: int) -> int:
+        return cls.lib().orc_splitmix64(seed, draw)
 
     @classmethod
     def uniform(cls, rng: int, seed: int, draw: int) -> float:

@@ -1,0 +1,87 @@
+"""Shared fixtures.  `-m "not gpu"` runs the oracle pins, host logic and ABI
+checks on CPU; `-m gpu` runs the parity tests through the C-ABI on a B200."""
+from __future__ import annotations
+
+import importlib
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+CACHE = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
+
+mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 and the built CUDA library")
+    config.addinivalue_line("markers", "slow: long-running parity case")
+
+
+def golden(name: str):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def synthetic_bundle(seed: int, layers: int, mask_stop: bool, expect_sha: str | None = None) -> str:
+    path = os.path.join(CACHE, f"gpt_s{seed}_l{layers}_m{int(mask_stop)}")
+    sha = mit2.write_synthetic_gpt_bundle(path, seed=seed, layers=layers, mask_stop=mask_stop)
+    if expect_sha is not None and sha != expect_sha:
+        raise RuntimeError(f"synthetic bundle {path} does not reproduce the fixture's weights "
+                           f"(sha {sha} != {expect_sha})")
+    return path
+
+
+@pytest.fixture(scope="session")
+def full_bundle():
+    g = golden("gpt_full.npz")
+    return synthetic_bundle(42, 24, False, str(g["bundle_sha256"]))
+
+
+@pytest.fixture(scope="session")
+def long_bundle():
+    g = golden("gpt_long.npz")
+    return synthetic_bundle(42, 24, True, str(g["bundle_sha256"]))
+
+
+@pytest.fixture(scope="session")
+def shallow_bundle():
+    return synthetic_bundle(7, 2, False)
+
+
+@pytest.fixture(scope="session")
+def shallow_masked_bundle():
+    return synthetic_bundle(8, 2, True)
+
+
+@pytest.fixture(scope="session")
+def oracle_mod():
+    import oracle as O
+    if not os.path.exists(O.PORT_SO):
+        O.build(ref=False)
+    return O
+
+
+@pytest.fixture(scope="session")
+def gpt_mod():
+    return importlib.import_module("index-tts-25-metal_b200.gpt")
+
+
+def conditioning(seed, n_text, text_hi=12000):
+    r = np.random.default_rng(seed)
+    spk = r.standard_normal(192).astype(np.float32)
+    emo = r.standard_normal(1280).astype(np.float32)
+    ids = r.integers(2, text_hi, n_text).astype(np.uint32)
+    return spk, emo, ids
+
+
+def latent_prefix(prepare, seed, n_latents, n_text, language=3):
+    """n_latents N(0,1) conditioning rows + the text and start rows of prepare()."""
+    spk, emo, ids = conditioning(seed, n_text)
+    p = prepare(spk, emo, ids, language)
+    lat = np.random.default_rng(seed + 1).standard_normal((n_latents, 1280)).astype(np.float32)
+    return np.concatenate([lat, p[3:]], 0)

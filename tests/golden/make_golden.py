@@ -1,0 +1,159 @@
+"""Generates the golden fixtures under tests/golden/ from the REFERENCE's own
+GPT code (src/gpt.cpp, src/gpt_sampling.cpp, src/weights.cpp, bundle.cpp built
+against the CPU MetalContext shim: oracle/_ref/libitts_ref.so).
+
+Run here, where the reference tree exists:  python tests/golden/make_golden.py
+The fixtures record the synthetic bundle arguments and the SHA-256 of its
+weights.bin, so a test can re-create the identical bundle anywhere.
+
+Fixtures (all inputs seeded):
+  gpt_full.npz       24-layer bundle (seed 42): prepare for two languages,
+                     prefill logits, four teacher-forced step logits (the
+                     granularity of the reference's gpt_test, src/main.cpp:31-66),
+                     greedy codes (rp 1 and rp 10), 3-beam codes, sampled codes.
+  gpt_long.npz       24-layer bundle (seed 42, stop code masked): the config-1
+                     prefix (32 latents + 64 text ids) with 1024 greedy codes and
+                     the config-2 prefix (32 latents + 200 text ids) with 1024
+                     SplitMix64 sampled codes (T 0.8, k 30, p 0.8, rp 10, seed 1234).
+  processors.npz     apply_gpt_sampling_processors on seeded logits and history
+                     for several option sets (src/main.cpp:147-158 layout:
+                     [temperature, top_k, top_p, repetition_penalty, num_beams]).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+import oracle as O  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CACHE = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
+
+
+def bundle(seed, layers, mask_stop):
+    path = os.path.join(CACHE, f"gpt_s{seed}_l{layers}_m{int(mask_stop)}")
+    sha = mit2.write_synthetic_gpt_bundle(path, seed=seed, layers=layers, mask_stop=mask_stop)
+    return path, sha
+
+
+def conditioning(seed, n_text, text_hi=12000):
+    r = np.random.default_rng(seed)
+    spk = r.standard_normal(192).astype(np.float32)
+    emo = r.standard_normal(1280).astype(np.float32)
+    ids = r.integers(2, text_hi, n_text).astype(np.uint32)
+    return spk, emo, ids
+
+
+def latent_prefix(ref, seed, n_latents, n_text, language=3):
+    """Benchmark prefix: n_latents N(0,1) conditioning rows replace the three
+    conditioning rows of prepare(); then the text rows and the start row."""
+    spk, emo, ids = conditioning(seed, n_text)
+    p = ref.prepare(spk, emo, ids, language)
+    lat = np.random.default_rng(seed + 1).standard_normal((n_latents, 1280)).astype(np.float32)
+    return np.concatenate([lat, p[3:]], 0), ids
+
+
+def make_full(ref_path, sha, out):
+    ref = O.RefOracle(ref_path)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 0, "bundle_sha256": sha}
+    spk, emo, ids = conditioning(7, 10)
+    d["speaker"], d["emotion"], d["text"] = spk, emo, ids
+    for lang in (3, 41):
+        d[f"prefix.{lang}"] = ref.prepare(spk, emo, ids, lang)
+    prefix = d["prefix.3"]
+    d["decode.prefill.logits"] = ref.prefill(prefix)
+    codes = np.array([17, 4090, 812, 8000], np.uint32)
+    d["decode.codes"] = codes
+    for i in range(1, 5):
+        d[f"decode.{i}.logits"] = ref.step(int(codes[i - 1]), i)
+    d["decode.cached_tokens"] = np.uint32(ref.cached_tokens)
+    g1, s1 = ref.generate(prefix, O.make_opts(do_sample=False, repetition_penalty=1.0), 8)
+    d["generation.greedy.codes"], d["generation.greedy.stopped"] = g1, np.int32(s1)
+    g2, s2 = ref.generate(prefix, O.make_opts(do_sample=False), 32)
+    d["generation.greedy_rp10.codes"], d["generation.greedy_rp10.stopped"] = g2, np.int32(s2)
+    b, bs = ref.generate(prefix, O.make_opts(do_sample=False, repetition_penalty=1.0, num_beams=3), 8)
+    d["generation.beam.codes"], d["generation.beam.stopped"] = b, np.int32(bs)
+    sm, ss = ref.generate(prefix, O.make_opts(seed=99), 32)
+    d["generation.sampled.codes"], d["generation.sampled.stopped"] = sm, np.int32(ss)
+    np.savez_compressed(out, **d)
+    print("wrote", out, {k: v.shape for k, v in d.items() if hasattr(v, "shape")})
+
+
+def make_long(ref_path, sha, out, n_codes):
+    ref = O.RefOracle(ref_path)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 1, "bundle_sha256": sha}
+    p1, ids1 = latent_prefix(ref, 1001, 32, 64)
+    d["config1.text"] = ids1
+    d["config1.rows"] = np.uint32(p1.shape[0])
+    t = time.time()
+    c1, s1 = ref.generate(p1, O.make_opts(do_sample=False), n_codes)
+    print("config1 greedy", len(c1), time.time() - t, flush=True)
+    d["config1.greedy.codes"] = c1
+    p2, ids2 = latent_prefix(ref, 1002, 32, 200)
+    d["config2.text"] = ids2
+    d["config2.rows"] = np.uint32(p2.shape[0])
+    t = time.time()
+    c2, s2 = ref.generate(p2, O.make_opts(seed=1234), n_codes)
+    print("config2 sampled", len(c2), time.time() - t, flush=True)
+    d["config2.sampled.codes"] = c2
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+PROCESSOR_CASES = {
+    # name: [temperature, top_k, top_p, repetition_penalty, num_beams]
+    "standard": [0.8, 30, 0.8, 10.0, 1],
+    "beam": [1.0, 0, 1.0, 10.0, 3],
+    "beam_edge": [0.7, 1, 0.05, 2.0, 3],
+    "unfiltered": [1.0, 0, 1.0, 1.0, 1],
+    "topp_only": [1.3, 0, 0.6, 1.0, 1],
+    "topk_only": [0.5, 50, 1.0, 1.5, 1],
+    "ties": [1.0, 5, 0.9, 1.0, 1],
+}
+
+
+def make_processors(out):
+    r = np.random.default_rng(5)
+    logits = (r.standard_normal(8194) * 2.0).astype(np.float32)
+    history = np.concatenate([[1, 8192], r.integers(0, 8194, 40), [9000, 1, 17]]).astype(np.uint32)
+    tie_logits = np.round(logits * 4) / 4  # many exact ties around the k-th value
+    d = {"logits": logits, "tie_logits": tie_logits.astype(np.float32), "history": history}
+    for name, (t, k, p, rp, nb) in PROCESSOR_CASES.items():
+        opts = O.make_opts(temperature=t, top_k=k, top_p=p, repetition_penalty=rp, num_beams=nb)
+        src = d["tie_logits"] if name == "ties" else logits
+        s = O.RefOracle.apply_processors(src, history, opts)
+        d[f"{name}.config"] = np.array([t, k, p, rp, nb], np.float32)
+        d[f"{name}.allowed"] = np.isfinite(s).astype(np.uint8)
+        d[f"{name}.values"] = np.where(np.isfinite(s), s, 0).astype(np.float32)
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", choices=["full", "long", "processors"], default=None)
+    ap.add_argument("--long-codes", type=int, default=1024)
+    a = ap.parse_args()
+    if not O.RefOracle.available():
+        O.build(ref=True)
+    if a.only in (None, "processors"):
+        make_processors(os.path.join(HERE, "processors.npz"))
+    if a.only in (None, "full"):
+        path, sha = bundle(42, 24, False)
+        make_full(path, sha, os.path.join(HERE, "gpt_full.npz"))
+    if a.only in (None, "long"):
+        path, sha = bundle(42, 24, True)
+        make_long(path, sha, os.path.join(HERE, "gpt_long.npz"), a.long_codes)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,275 @@
+"""Parity of the CUDA library (through the C-ABI) with the reference.
+
+* Full 24-layer model (seed 42) against fixtures produced by the reference's
+  own gpt.cpp / gpt_sampling.cpp: the granularity of the reference's gpt_test
+  (src/main.cpp:31-66) -- prepare, prefill logits, four teacher-forced steps,
+  greedy and beam codes -- plus sampled codes and two 1024-code runs.
+* Shallow (2-layer) models against the live CPU oracle (oracle/gpt_port.cpp)
+  for prefix lengths 1..1024, long KV contexts and option sweeps.
+Tolerances: logits use the reference comparator (max_abs < 1e-4, RMSE < 2e-5,
+src/main.cpp:44-48) together with the 1e-4 relative bound of the fp32 target
+and an exact argmax; codes, allowed masks and processor values are exact."""
+import numpy as np
+import pytest
+
+from conftest import golden, latent_prefix
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_MAX_ABS = 1e-4
+LOGIT_RMSE = 2e-5
+LOGIT_REL = 1e-4
+
+
+def assert_logits_close(actual, expected, what=""):
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert np.isfinite(a).all(), what
+    d = np.abs(a - e)
+    rmse = float(np.sqrt((d * d).mean()))
+    scale = max(1.0, float(np.abs(e).max()))
+    assert d.max() < LOGIT_MAX_ABS, f"{what}: max_abs {d.max():.3e}"
+    assert d.max() <= LOGIT_REL * scale, f"{what}: relative {d.max() / scale:.3e}"
+    assert rmse < LOGIT_RMSE, f"{what}: rmse {rmse:.3e}"
+    assert int(a.argmax()) == int(e.argmax()), f"{what}: argmax {a.argmax()} != {e.argmax()}"
+
+
+@pytest.fixture(scope="module")
+def dec_full(gpt_mod, full_bundle):
+    d = gpt_mod.GptDecoder(full_bundle)
+    yield d
+    d.close()
+
+
+@pytest.fixture(scope="module")
+def dec_long(gpt_mod, long_bundle):
+    d = gpt_mod.GptDecoder(long_bundle)
+    yield d
+    d.close()
+
+
+@pytest.fixture(scope="module")
+def dec_shallow(gpt_mod, shallow_bundle):
+    d = gpt_mod.GptDecoder(shallow_bundle)
+    yield d
+    d.close()
+
+
+@pytest.fixture(scope="module")
+def port_shallow(oracle_mod, shallow_bundle):
+    return oracle_mod.PortOracle(shallow_bundle)
+
+
+# ------------------------------------------------------------------ full model
+def test_info(dec_full):
+    i = dec_full.info()
+    assert i.layers == 24 and i.mel_pos_rows == 1818 and i.sm_count >= 100
+    assert i.stream_bytes == 1931051016
+
+
+def test_prepare_matches_reference(dec_full):
+    g = golden("gpt_full.npz")
+    for lang in (3, 41):
+        p = dec_full.prepare(g["speaker"], g["emotion"], g["text"], lang)
+        e = g[f"prefix.{lang}"]
+        assert p.shape == e.shape
+        np.testing.assert_array_equal(p[1:], e[1:])  # pure float adds: exact
+        np.testing.assert_allclose(p[0], e[0], atol=1e-5, rtol=0)  # 192-term projection
+
+
+def test_prefill_and_steps_match_reference(dec_full):
+    g = golden("gpt_full.npz")
+    assert_logits_close(dec_full.prefill(g["prefix.3"]), g["decode.prefill.logits"], "prefill")
+    for i in range(1, 5):
+        assert_logits_close(dec_full.step(int(g["decode.codes"][i - 1]), i), g[f"decode.{i}.logits"], f"decode.{i}")
+    assert dec_full.cached_tokens() == int(g["decode.cached_tokens"])
+
+
+@pytest.mark.parametrize("name,kw,n", [
+    ("greedy", dict(do_sample=False, repetition_penalty=1.0), 8),
+    ("greedy_rp10", dict(do_sample=False), 32),
+    ("beam", dict(do_sample=False, repetition_penalty=1.0, num_beams=3), 8),
+    ("sampled", dict(seed=99), 32),
+])
+def test_generation_matches_reference(dec_full, gpt_mod, name, kw, n):
+    g = golden("gpt_full.npz")
+    r = dec_full.generate(g["prefix.3"], gpt_mod.gen_opts(**kw), n)
+    np.testing.assert_array_equal(r.codes, g[f"generation.{name}.codes"])
+    assert r.stopped == bool(g[f"generation.{name}.stopped"])
+
+
+def test_greedy_1024_codes_bit_identical(dec_long, gpt_mod):
+    g = golden("gpt_long.npz")
+    prefix = latent_prefix(dec_long.prepare, 1001, 32, 64)
+    assert prefix.shape[0] == int(g["config1.rows"])
+    r = dec_long.generate(prefix, gpt_mod.gen_opts(do_sample=False), 1024)
+    np.testing.assert_array_equal(r.codes, g["config1.greedy.codes"])
+    assert dec_long.cached_tokens() == prefix.shape[0] + 1023
+
+
+def test_sampled_1024_codes_match_reference(dec_long, gpt_mod):
+    g = golden("gpt_long.npz")
+    prefix = latent_prefix(dec_long.prepare, 1002, 32, 200)
+    r = dec_long.generate(prefix, gpt_mod.gen_opts(seed=1234), 1024)
+    np.testing.assert_array_equal(r.codes, g["config2.sampled.codes"])
+
+
+@pytest.mark.parametrize("case", ["standard", "beam", "beam_edge", "unfiltered", "topp_only", "topk_only", "ties"])
+def test_processors_match_reference(dec_full, gpt_mod, case):
+    g = golden("processors.npz")
+    t, k, p, rp, nb = g[f"{case}.config"].tolist()
+    opts = gpt_mod.gen_opts(temperature=t, top_k=int(k), top_p=p, repetition_penalty=rp, num_beams=int(nb))
+    src = g["tie_logits"] if case == "ties" else g["logits"]
+    s = dec_full.apply_processors(src, g["history"], opts)
+    allowed = np.isfinite(s)
+    np.testing.assert_array_equal(allowed, g[f"{case}.allowed"].astype(bool))
+    np.testing.assert_array_equal(np.where(allowed, s, 0), g[f"{case}.values"])
+
+
+# ---------------------------------------------------------- shallow vs oracle
+@pytest.mark.parametrize("rows", [1, 2, 33, 257, 1024])
+def test_prefill_lengths_match_oracle(dec_shallow, port_shallow, rows):
+    prefix = np.random.default_rng(rows).standard_normal((rows, 1280)).astype(np.float32)
+    assert_logits_close(dec_shallow.prefill(prefix), port_shallow.prefill(prefix), f"prefill rows={rows}")
+    for i, code in enumerate([5, 8192, 4000]):
+        assert_logits_close(dec_shallow.step(code, i + 2), port_shallow.step(code, i + 2), f"step {i} rows={rows}")
+
+
+@pytest.mark.parametrize("kw", [
+    dict(do_sample=False),
+    dict(do_sample=False, repetition_penalty=1.0),
+    dict(seed=5),
+    dict(seed=6, rng=1),
+    dict(seed=7, temperature=1.3, top_k=0, top_p=0.5),
+    dict(seed=8, top_k=3, top_p=1.0, repetition_penalty=1.0),
+    dict(seed=9, top_k=0, top_p=1.0, temperature=0.9),
+])
+def test_generate_options_match_oracle(dec_shallow, port_shallow, gpt_mod, oracle_mod, kw):
+    prefix = np.random.default_rng(11).standard_normal((40, 1280)).astype(np.float32)
+    r = dec_shallow.generate(prefix, gpt_mod.gen_opts(**kw), 48)
+    e, st = port_shallow.generate(prefix, oracle_mod.make_opts(**kw), 48)
+    np.testing.assert_array_equal(r.codes, e)
+    assert r.stopped == st
+
+
+def test_stop_code_ends_generation(gpt_mod, oracle_mod, shallow_bundle):
+    """A bundle whose mel_head favours the stop code: the loop stops and the
+    stop code is not returned (gpt_sampling.cpp:181)."""
+    import os
+    import shutil
+    from conftest import CACHE, mit2
+    path = os.path.join(CACHE, "gpt_s7_l2_stopbias")
+    if not mit2.bundle_complete(path):
+        os.makedirs(path, exist_ok=True)
+        shutil.copy(os.path.join(shallow_bundle, "manifest.json"), path)
+        shutil.copy(os.path.join(shallow_bundle, "weights.bin"), path)
+        b = mit2.Bundle(path)
+        t = b.tensors["gpt.mel_head.bias"]
+        with open(os.path.join(path, "weights.bin"), "r+b") as f:
+            f.seek(t.offset + 8193 * 4)
+            f.write(np.float32(30.0).tobytes())
+        open(os.path.join(path, ".complete"), "w").write("{}")
+    dec = gpt_mod.GptDecoder(path)
+    port = oracle_mod.PortOracle(path)
+    prefix = np.random.default_rng(3).standard_normal((10, 1280)).astype(np.float32)
+    r = dec.generate(prefix, gpt_mod.gen_opts(do_sample=False), 20)
+    e, st = port.generate(prefix, oracle_mod.make_opts(do_sample=False), 20)
+    assert r.stopped and st and len(r.codes) == len(e) == 0
+    assert dec.cached_tokens() == 10
+    dec.close()
+
+
+@pytest.mark.slow
+def test_long_context_steps_match_oracle(dec_shallow, port_shallow):
+    """Steps up to 3900 cached keys (split-K chunks at their 512-key cap)."""
+    prefix = np.random.default_rng(99).standard_normal((1024, 1280)).astype(np.float32)
+    assert_logits_close(dec_shallow.prefill(prefix), port_shallow.prefill(prefix), "prefill 1024")
+    rng = np.random.default_rng(5)
+    codes = rng.integers(0, 8192, 2880)
+    for i, c in enumerate(codes):
+        pos = 2 + i % 1800
+        a = dec_shallow.step(int(c), pos)
+        b = port_shallow.step(int(c), pos)
+        if i % 480 == 0 or i == len(codes) - 1:
+            assert_logits_close(a, b, f"step {i} (cached {1024 + i})")
+    assert dec_shallow.cached_tokens() == 1024 + 2880
+
+
+def test_layered_mode_matches_persistent(dec_shallow, gpt_mod):
+    prefix = np.random.default_rng(4).standard_normal((70, 1280)).astype(np.float32)
+    outs = []
+    for mode in (0, 1):
+        dec_shallow.set_decode_mode(mode)
+        l0 = dec_shallow.prefill(prefix)
+        steps = [dec_shallow.step(c, 2 + i) for i, c in enumerate([3, 99, 8000])]
+        r = dec_shallow.generate(prefix, gpt_mod.gen_opts(seed=3), 24)
+        outs.append((l0, steps, r.codes))
+    dec_shallow.set_decode_mode(0)
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    for a, b in zip(outs[0][1], outs[1][1]):
+        np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(outs[0][2], outs[1][2])
+
+
+def test_checkpoint_restore_round_trip(dec_shallow):
+    prefix = np.random.default_rng(8).standard_normal((30, 1280)).astype(np.float32)
+    dec_shallow.prefill(prefix)
+    dec_shallow.step(10, 2)
+    st = dec_shallow.checkpoint()
+    a = dec_shallow.step(20, 3)
+    b = dec_shallow.step(30, 4)
+    dec_shallow.restore(st)
+    assert dec_shallow.cached_tokens() == 31
+    np.testing.assert_array_equal(dec_shallow.step(20, 3), a)
+    np.testing.assert_array_equal(dec_shallow.step(30, 4), b)
+
+
+def test_device_resident_api_matches_host_api(dec_shallow, gpt_mod):
+    import torch
+    prefix = np.random.default_rng(12).standard_normal((50, 1280)).astype(np.float32)
+    opts = gpt_mod.gen_opts(seed=21)
+    ref = dec_shallow.generate(prefix, opts, 40)
+    d_prefix = torch.from_numpy(prefix).cuda()
+    d_codes = torch.zeros(40, dtype=torch.int32, device="cuda")
+    d_info = torch.zeros(4, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    dec_shallow.prefill_async(d_prefix.data_ptr(), 50)
+    dec_shallow.decode_async(opts, 40, d_codes.data_ptr(), d_info.data_ptr())
+    dec_shallow.sync()
+    info = d_info.cpu().numpy()
+    assert info[0] == 40 and info[1] == 0 and info[2] == 0 and info[3] == 39
+    np.testing.assert_array_equal(d_codes.cpu().numpy().astype(np.uint32), ref.codes)
+    assert dec_shallow.cached_tokens() == 50 + 39
+
+
+def test_errors_match_reference_and_leave_context_usable(dec_shallow, gpt_mod):
+    G = gpt_mod
+    with pytest.raises(ValueError):
+        dec_shallow.prefill(np.zeros(1281, np.float32))
+    with pytest.raises(ValueError):
+        dec_shallow.prefill(np.zeros((1025, 1280), np.float32))
+    prefix = np.random.default_rng(1).standard_normal((4, 1280)).astype(np.float32)
+    dec_shallow.prefill(prefix)
+    with pytest.raises(ValueError):
+        dec_shallow.step(8194, 2)
+    with pytest.raises(ValueError):
+        dec_shallow.step(5, 1818)
+    with pytest.raises(ValueError):
+        dec_shallow.generate(prefix, G.gen_opts(temperature=0.0), 4)
+    with pytest.raises(ValueError):
+        dec_shallow.generate(prefix, G.gen_opts(num_beams=0), 4)
+    with pytest.raises(ValueError):
+        dec_shallow.generate(prefix, G.gen_opts(), 0)
+    with pytest.raises(ValueError):
+        dec_shallow.generate(prefix, G.gen_opts(), 1817)
+    with pytest.raises(ValueError):
+        dec_shallow.prepare(np.zeros(191), np.zeros(1280), [5], 3)
+    with pytest.raises(ValueError):
+        dec_shallow.prepare(np.zeros(192), np.zeros(1280), [60510], 3)
+    with pytest.raises(ValueError):
+        dec_shallow.prepare(np.zeros(192), np.zeros(1280), [5], 107)
+    with pytest.raises(RuntimeError):
+        dec_shallow.apply_processors(np.zeros(8194), [], G.gen_opts(temperature=-1.0))
+    # still usable
+    r = dec_shallow.generate(prefix, G.gen_opts(do_sample=False), 4)
+    assert len(r.codes) == 4
