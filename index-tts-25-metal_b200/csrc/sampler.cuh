@@ -273,7 +273,13 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
             if (s[k] < pivot) s[k] = -INFINITY;
     }
     const bool top_p = o.top_p < 1.0f;
-    if (!top_p && !out_scores && greedy) return block_argmax(s, base, cnt, sm);
+    if (!top_p && out_scores) {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+            if (k < cnt) out_scores[base + k] = s[k];
+        return 0;
+    }
+    if (!top_p && greedy) return block_argmax(s, base, cnt, sm);
 
     // finite survivors in index order
     uint32_t nf = 0;

@@ -270,6 +270,11 @@ def test_errors_match_reference_and_leave_context_usable(dec_shallow, gpt_mod):
         dec_shallow.prepare(np.zeros(192), np.zeros(1280), [5], 107)
     with pytest.raises(RuntimeError):
         dec_shallow.apply_processors(np.zeros(8194), [], G.gen_opts(temperature=-1.0))
+    # all scores -inf: returned unchanged without top-p, an error with it (gpt_sampling.cpp:69-91)
+    inf = np.full(8194, -np.inf, np.float32)
+    assert np.isneginf(dec_shallow.apply_processors(inf, [], G.gen_opts(top_k=0, top_p=1.0))).all()
+    with pytest.raises(RuntimeError):
+        dec_shallow.apply_processors(inf, [], G.gen_opts(top_k=0, top_p=0.5))
     # still usable
     r = dec_shallow.generate(prefix, G.gen_opts(do_sample=False), 4)
     assert len(r.codes) == 4
