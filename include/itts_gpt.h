@@ -104,7 +104,7 @@ void itts_gen_opts_default(itts_gen_opts* opts);
  * count is taken from the bundle (1..24); the reference requires 24. */
 int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_gpt_ctx** out);
 void itts_gpt_destroy(itts_gpt_ctx* ctx);
-const char* itts_gpt_last_error(const itts_gpt_ctx* ctx);
+const char* itts_gpt_last_error(const itts_gpt_ctx* ctx);  /* NULL: this thread's last create / noalloc error */
 int itts_gpt_get_info(const itts_gpt_ctx* ctx, itts_gpt_info* info);
 
 /* ---- GptDecoder::prepare (gpt.cpp:42-71) ----------------------------------
@@ -163,6 +163,23 @@ int itts_gpt_sync(itts_gpt_ctx* ctx);
  * phase, same device code).  Counters: kernel launches issued by the context. */
 int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode);
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx);
+
+/* ---- allocation-free processors --------------------------------------------
+ * No counterpart in the reference.  The logits processors of
+ * itts_gpt_apply_processors for callers that cannot allocate device memory:
+ * a thread inside a CUDA stream capture (allocation is illegal there), a
+ * latency-critical serving thread (cudaMalloc/cudaFree can synchronise the
+ * device) or a process whose device memory is fully reserved elsewhere.  It
+ * needs no context and calls no cudaMalloc/cudaFree: inputs and outputs are
+ * host arrays staged through one static device array of 133,136 bytes that
+ * every GPU loading this library holds until exit.  history_n is limited to
+ * 16384 tokens (larger values return ITTS_ERR_INVALID_ARGUMENT).  The first
+ * call on a device looks up that array's address; make it before any stream
+ * capture.  All calls share the array: calls that overlap on one GPU (from two
+ * host threads) race, so serialise them.  Errors are reported by
+ * itts_gpt_last_error(NULL) on the calling thread. */
+int itts_gpt_apply_processors_noalloc(int device, const float* logits, size_t n, const uint32_t* history,
+                                      size_t history_n, const itts_gen_opts* opts, float* out);
 
 #ifdef __cplusplus
 }

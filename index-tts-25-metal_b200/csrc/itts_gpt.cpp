@@ -646,6 +646,10 @@ std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n
 
 }  // namespace
 
+namespace itts {
+void set_thread_error(const std::string& msg) { g_create_error = msg; }
+}  // namespace itts
+
 // ================================================================ C-ABI
 extern "C" {
 

@@ -83,6 +83,8 @@ SIGNATURES = {
     "itts_gpt_sync": (C.c_int, [_P]),
     "itts_gpt_set_decode_mode": (C.c_int, [_P, C.c_int]),
     "itts_gpt_launch_count": (C.c_uint64, [_P]),
+    "itts_gpt_apply_processors_noalloc": (C.c_int, [C.c_int, _P, C.c_size_t, _P, C.c_size_t, C.POINTER(GenOpts),
+                                                    _P]),
 }
 
 _lib = None
@@ -269,3 +271,19 @@ class GptDecoder:
 
     def sync(self):
         self._check(self._lib.itts_gpt_sync(self._h))
+
+
+NOALLOC_MAX_HISTORY = 16384
+
+
+def apply_processors_noalloc(logits, history, options: GenOpts, device: int = 0) -> np.ndarray:
+    """itts_gpt_apply_processors_noalloc: the processors without a context and
+    without any device allocation (see include/itts_gpt.h)."""
+    lib = load_library()
+    lg, hist = _f32(logits), _u32(history)
+    out = np.empty_like(lg)
+    rc = lib.itts_gpt_apply_processors_noalloc(device, _ptr(lg), lg.size, _ptr(hist), hist.size, C.byref(options),
+                                               _ptr(out))
+    if rc != OK:
+        _raise(rc, lib.itts_gpt_last_error(None).decode())
+    return out
