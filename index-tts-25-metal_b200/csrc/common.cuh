@@ -97,6 +97,42 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return warp_max(t);
 }
 
+// Named barrier 1 over the kThreads consumer threads of a CTA: every thread of
+// a kernel launched with kThreads, or the 16 consumer warps of the decode
+// kernels, whose extra producer warp never joins it.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
+// csync() that also ORs a predicate across the consumer threads.
+__device__ __forceinline__ bool csync_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.or.pred po, 1, %2, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "n"(kThreads)
+        : "memory");
+    return r != 0;
+}
+
+// Sum / max over the kThreads consumer threads (two csync()).
+__device__ __forceinline__ float cblock_sum(float v, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    csync();
+    if (lane == 0) red[warp] = v;
+    csync();
+    return warp_sum(lane < kWarps ? red[lane] : 0.0f);
+}
+
+__device__ __forceinline__ float cblock_max(float v, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_max(v);
+    csync();
+    if (lane == 0) red[warp] = v;
+    csync();
+    return warp_max(lane < kWarps ? red[lane] : -INFINITY);
+}
+
 __device__ __forceinline__ void set_status(int* status, int code, int where, int detail) {
     if (atomicCAS(status, 0, code) == 0) {
         status[1] = where;

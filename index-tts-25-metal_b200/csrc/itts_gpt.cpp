@@ -98,6 +98,7 @@ struct itts_gpt_ctx {
     uint32_t* d_hist = nullptr;     // processor history (grown on demand)
     size_t d_hist_cap = 0;
     float* d_beam = nullptr;        // beam logits slots + scores
+    void* d_sampler_big = nullptr;  // per-CTA sampler workspace
     uint32_t beam_cap = 0;
     float* h_stage = nullptr;       // pinned [1024 * 1280]
     float* h_logits = nullptr;      // pinned [8194 * 10]
@@ -114,7 +115,7 @@ struct itts_gpt_ctx {
         if (stream) cudaStreamSynchronize(stream);
         for (void* p : {(void*)d_weights, (void*)d_model, (void*)d_kv, (void*)d_hidden, (void*)d_act,
                         (void*)d_history, (void*)d_codes, (void*)d_info, (void*)d_misc, (void*)d_hist,
-                        (void*)d_beam})
+                        (void*)d_beam, d_sampler_big})
             if (p) cudaFree(p);
         for (void* p : {(void*)h_stage, (void*)h_logits, (void*)h_codes, (void*)h_ctl})
             if (p) cudaFreeHost(p);
@@ -217,6 +218,13 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
                                  "mlp.c_fc.weight", "mlp.c_fc.bias", "mlp.c_proj.weight", "mlp.c_proj.bias"};
     for (uint32_t i = 0; i < layers; ++i)
         for (const char* n : per_layer) idx.push_back(add("gpt.gpt.h." + std::to_string(i) + "." + n));
+    // mlp.c_proj is also kept in its bundle layout [5120, 1280] for the decode
+    // split-K product; the transposed copy serves the prefill GEMM.
+    std::vector<size_t> mpT_off(layers);
+    for (uint32_t i = 0; i < layers; ++i) {
+        mpT_off[i] = total;
+        total += align256(size_t(5120) * 1280 * 4);
+    }
     c->d_weights = dev_alloc<char>(total, "weight allocation");
     c->weight_bytes = total;
 
@@ -229,6 +237,11 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
             const bool is_conv = t.name.rfind("gpt.gpt.h.", 0) == 0 && t.shape.size() == 2;
             if (is_conv) {
                 ck(cudaMemcpy(stage, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+                const std::string suffix = ".mlp.c_proj.weight";
+                if (t.name.size() > suffix.size() && t.name.compare(t.name.size() - suffix.size(), suffix.size(), suffix) == 0) {
+                    const uint32_t li = uint32_t(std::stoul(t.name.substr(10, t.name.find('.', 10) - 10)));
+                    ck(cudaMemcpy(c->d_weights + mpT_off[li], stage, t.nbytes, cudaMemcpyDeviceToDevice), "weight copy");
+                }
                 ck(itts::launch_transpose(stage, reinterpret_cast<float*>(dst), int(t.shape[0]), int(t.shape[1]),
                                           nullptr),
                    "transpose launch");
@@ -272,6 +285,7 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
         L.b_fc = ptr(o + 9);
         L.w_mp = ptr(o + 10);
         L.b_mp = ptr(o + 11);
+        L.w_mpT = reinterpret_cast<const float*>(c->d_weights + mpT_off[i]);
     }
     const uint64_t per_layer_floats = 19660800ull + 11520ull + 5120ull;
     c->stream_bytes = 4ull * (per_layer_floats * layers + 10488320ull + 8194ull + 5120ull + 2560ull);
@@ -288,26 +302,29 @@ void alloc_buffers(itts_gpt_ctx* c) {
     c->d_r = c->d_att + T * kW;
     c->d_qkv = c->d_r + T * kW;
     c->d_ff = c->d_qkv + T * 3840;
-    // decode activations (each region 256-byte aligned)
-    const size_t sizes[8] = {kW, 3840, kW, kW, 5120, 8448, size_t(kH) * 128 * 66, 64};
+    // decode activations (each region 256-byte aligned): qkv, r[2], acc[2]
+    // (8-byte), logits, attention partials, control block
+    const size_t sizes[6] = {3840 * 4, 2 * kW * 4, 2 * kW * 8, 8448 * 4, size_t(kH) * 256 * 66 * 4,
+                             sizeof(itts::DecodeCtl)};
     size_t total = 0;
-    for (size_t s : sizes) total += align256(s * 4);
+    for (size_t s : sizes) total += align256(s);
     c->d_act = reinterpret_cast<float*>(dev_alloc<char>(total, "decode buffers"));
     char* p = reinterpret_cast<char*>(c->d_act);
-    float* regions[8];
-    for (int i = 0; i < 8; ++i) {
-        regions[i] = reinterpret_cast<float*>(p);
-        p += align256(sizes[i] * 4);
+    char* regions[6];
+    for (int i = 0; i < 6; ++i) {
+        regions[i] = p;
+        p += align256(sizes[i]);
     }
     c->db.kv = c->d_kv;
-    c->db.h = regions[0];
-    c->db.qkv = regions[1];
-    c->db.attn = regions[2];
-    c->db.r = regions[3];
-    c->db.ff = regions[4];
-    c->db.logits = regions[5];
-    c->db.part = regions[6];
-    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[7]);
+    c->db.qkv = reinterpret_cast<float*>(regions[0]);
+    c->db.r = reinterpret_cast<float*>(regions[1]);
+    c->db.acc = reinterpret_cast<long long*>(regions[2]);
+    c->db.logits = reinterpret_cast<float*>(regions[3]);
+    c->db.part = reinterpret_cast<float*>(regions[4]);
+    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[5]);
+    c->db.sampler_big = reinterpret_cast<itts::SamplerBig*>(
+        dev_alloc<char>(size_t(c->sm_count) * itts::sampler_big_bytes(), "sampler workspace"));
+    c->d_sampler_big = c->db.sampler_big;
     ck(cudaMemset(c->d_act, 0, total), "decode buffer init");
     c->d_history = dev_alloc<uint32_t>(2, "history");
     const uint32_t hist[2] = {1, 8192};
@@ -365,6 +382,8 @@ itts::DecodeArgs decode_args(itts_gpt_ctx* c) {
 
 void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     reset_ctl(c);
+    // the first layer of a launch accumulates its mlp.c_proj sums into slot 0
+    ck(cudaMemsetAsync(c->db.acc, 0, 2 * kW * sizeof(long long), c->stream), "accumulator reset");
     if (c->mode == 0) {
         ck(itts::launch_decode_persistent(a, c->sm_count, c->stream), "persistent decode launch");
         ++c->launches;
@@ -377,10 +396,10 @@ void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
     itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x, c->d_qkv, c->d_att, c->d_r, c->d_ff, c->d_kv, int(rows)};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
-    ck(cudaMemcpyAsync(c->db.h, c->d_hidden + size_t(rows - 1) * kW, kW * 4, cudaMemcpyDeviceToDevice, c->stream),
-       "last row copy");
     reset_ctl(c);
-    ck(itts::launch_head(decode_args(c), c->sm_count, c->stream), "head launch");
+    itts::DecodeArgs a = decode_args(c);
+    a.head_src = c->d_hidden + size_t(rows - 1) * kW;
+    ck(itts::launch_head(a, c->sm_count, c->stream), "head launch");
     ++c->launches;
 }
 

@@ -16,6 +16,7 @@ enum DeviceStatus : int {
     kStatusInvalidCode = 2,      // sampled code 8192 (gpt_sampling.cpp:182)
     kStatusNoFiniteLogits = 3,   // sampling/top-p saw no finite score
     kStatusZeroMass = 4,         // probability mass was zero
+    kStatusRingTimeout = 5,      // a weight-ring slot did not arrive in time
 };
 
 
@@ -28,7 +29,8 @@ struct LayerW {
     const float *w_o, *b_o;      // [1280, 1280]
     const float *ln2_g, *ln2_b;
     const float *w_fc, *b_fc;    // [5120, 1280]
-    const float *w_mp, *b_mp;    // [1280, 5120]
+    const float *w_mp, *b_mp;    // [1280, 5120] (prefill GEMM)
+    const float *w_mpT;          // [5120, 1280]: the bundle's Conv1D layout (decode split-K)
 };
 
 struct ModelW {
@@ -63,16 +65,17 @@ struct DecodeCtl {
     unsigned pad[5];
 };
 
+struct SamplerBig;
+
 // Decode-time device buffers (activations live in L2; KV cache in HBM).
 struct DecodeBuffers {
     float* kv;        // [layer][K|V][head][4096][64] fp32
-    float* h;         // residual stream [1280]
     float* qkv;       // [3840]
-    float* attn;      // [1280]
-    float* r;         // [1280]
-    float* ff;        // [5120]
+    float* r;         // [2][1280] residual after attention, by layer parity
+    long long* acc;   // [2][1280] mlp.c_proj sums, 2^-32 fixed point, by layer parity
     float* logits;    // [8194]
-    float* part;      // split-K partials [20 * 512 * 66]
+    float* part;      // split-K attention partials [20 * 256 * 66]
+    SamplerBig* sampler_big;  // one large-survivor workspace per CTA
     DecodeCtl* ctl;
 };
 
@@ -91,10 +94,12 @@ struct DecodeArgs {
     uint32_t history_n;
     uint32_t* codes;      // kModeGenerate output [n_iter]
     uint32_t* info_out;   // optional copy of ctl->info (may be null)
+    const float* head_src;  // prefill: last hidden row fed to the head phase
 };
 
 // ---- host-side launchers (decode.cu, prefill.cu, misc.cu) -----------------
 size_t decode_smem_bytes();
+size_t sampler_big_bytes();
 cudaError_t decode_configure(int* blocks_per_sm);
 cudaError_t launch_decode_persistent(const DecodeArgs& a, int ncta, cudaStream_t s);
 cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cudaStream_t s, uint64_t* launches);

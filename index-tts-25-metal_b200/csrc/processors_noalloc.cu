@@ -47,11 +47,15 @@ constexpr size_t kNoAllocScratchBytes = sizeof(NoAllocScratch);  // 133,136 byte
 // device address comes from cudaGetSymbolAddress (see scratch_on()).
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
+size_t sampler_dyn_smem_bytes();
+constexpr size_t kSmallBytes = (sizeof(SamplerSmem) + 15) & ~size_t(15);
+
 __global__ void __launch_bounds__(kThreads, 1) k_processors_noalloc(NoAllocScratch* s, SampleOpts o, uint32_t hist_n) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(smem_raw);
+    SamplerBig* big = reinterpret_cast<SamplerBig*>(smem_raw + kSmallBytes);
     sampler_init_seen(sm, s->history, hist_n);
-    run_sampler(s->logits, o, 0, false, sm, s->scores, s->status);
+    run_sampler(s->logits, o, 0, false, sm, big, s->scores, s->status);
 }
 
 namespace {
@@ -66,7 +70,7 @@ cudaError_t scratch_on(int device, NoAllocScratch** out) {
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(k_processors_noalloc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)sizeof(SamplerSmem));
+                                 (int)sampler_dyn_smem_bytes());
         if (e != cudaSuccess) return e;
         g_scratch_ptr[device] = static_cast<NoAllocScratch*>(p);
     }
@@ -120,7 +124,7 @@ extern "C" int itts_gpt_apply_processors_noalloc(int device, const float* logits
         ck(cudaMemset(s->status, 0, sizeof(s->status)), "status clear")) {
         const SampleOpts o{opts->do_sample, opts->top_k, opts->seed, opts->temperature, opts->top_p,
                            opts->repetition_penalty, opts->num_beams, opts->rng};
-        k_processors_noalloc<<<1, kThreads, sizeof(SamplerSmem)>>>(s, o, uint32_t(history_n));
+        k_processors_noalloc<<<1, kThreads, sampler_dyn_smem_bytes()>>>(s, o, uint32_t(history_n));
         int status[4] = {0, 0, 0, 0};
         if (ck(cudaGetLastError(), "processors launch") &&
             ck(cudaMemcpy(out, s->scores, kVocab * sizeof(float), cudaMemcpyDeviceToHost), "scores read") &&

@@ -30,7 +30,10 @@ namespace itts {
 constexpr int kPer = 17;
 constexpr int kBits = (kVocab + 31) / 32;
 constexpr int kSortCap = 16384;  // next power of two >= 8194
+constexpr int kFast = 256;       // survivors handled entirely in shared memory
 
+// Shared-memory part (~9.7 KB).  Up to kFast survivors are gathered, sorted and
+// their exp() values cached here; larger survivor sets use SamplerBig.
 struct SamplerSmem {
     uint32_t seen[kBits];
     uint32_t removed[kBits];
@@ -38,8 +41,18 @@ struct SamplerSmem {
     uint32_t scan[32];
     float redf[32];
     uint32_t redu[32];
-    uint32_t sel_bin, sel_rem, n_sv, result;
+    uint32_t sel_bin, sel_rem, result;
     int err;
+    uint32_t f_idx[kFast];
+    float f_s[kFast];
+    unsigned long long f_key[kFast];
+    double f_pr[kFast];
+};
+
+// Workspace for more than kFast survivors (top-p without top-k, or wide ties):
+// shared memory in single-CTA kernels, a per-CTA global slice in the
+// persistent decode kernel.
+struct SamplerBig {
     uint32_t sv_idx[kVocab];
     float sv_s[kVocab];
     unsigned long long key[kSortCap];
@@ -89,18 +102,18 @@ __device__ __forceinline__ bool bit_get(const uint32_t* b, uint32_t i) { return 
 // Seeds the repetition-penalty set with `hist` (tokens >= 8194 are ignored,
 // gpt_sampling.cpp:38-40).
 __device__ inline void sampler_init_seen(SamplerSmem& sm, const uint32_t* hist, uint32_t n) {
-    for (int i = threadIdx.x; i < kBits; i += blockDim.x) sm.seen[i] = 0;
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = threadIdx.x; i < kBits; i += kThreads) sm.seen[i] = 0;
+    csync();
+    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
         const uint32_t t = hist[i];
         if (t < (uint32_t)kVocab) atomicOr(&sm.seen[t >> 5], 1u << (t & 31));
     }
-    __syncthreads();
+    csync();
 }
 
 __device__ inline void sampler_mark_seen(SamplerSmem& sm, uint32_t t) {
     if (threadIdx.x == 0 && t < (uint32_t)kVocab) sm.seen[t >> 5] |= 1u << (t & 31);
-    __syncthreads();
+    csync();
 }
 
 // Exclusive block scan of v; *total receives the sum.  blockDim.x == kThreads.
@@ -112,9 +125,9 @@ __device__ inline uint32_t block_excl_scan(uint32_t v, SamplerSmem& sm, uint32_t
         const uint32_t n = __shfl_up_sync(0xffffffffu, inc, o);
         if (lane >= o) inc += n;
     }
-    __syncthreads();
+    csync();
     if (lane == 31) sm.scan[warp] = inc;
-    __syncthreads();
+    csync();
     if (warp == 0) {
         uint32_t w = lane < kWarps ? sm.scan[lane] : 0, wi = w;
 #pragma unroll
@@ -125,7 +138,7 @@ __device__ inline uint32_t block_excl_scan(uint32_t v, SamplerSmem& sm, uint32_t
         if (lane < kWarps) sm.scan[lane] = wi - w;
         if (lane == kWarps - 1) sm.redu[0] = wi;
     }
-    __syncthreads();
+    csync();
     *total = sm.redu[0];
     return sm.scan[warp] + inc - v;
 }
@@ -137,15 +150,15 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
-        __syncthreads();
+        for (int i = threadIdx.x; i < 256; i += kThreads) sm.hist[i] = 0;
+        csync();
 #pragma unroll
         for (int k = 0; k < kPer; ++k)
             if (k < cnt) {
                 const uint32_t key = ord_key(s[k]);
                 if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1u);
             }
-        __syncthreads();
+        csync();
         if (warp == 0) {
             uint32_t c[8], sum = 0;
 #pragma unroll
@@ -173,11 +186,11 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
                 }
             }
         }
-        __syncthreads();
+        csync();
         prefix |= sm.sel_bin << shift;
         mask |= 0xffu << shift;
         rem = sm.sel_rem;
-        __syncthreads();
+        csync();
     }
     return key_float(prefix);
 }
@@ -185,7 +198,7 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
 __device__ inline void bitonic_sort_asc(unsigned long long* key, int P) {
     for (int k = 2; k <= P; k <<= 1)
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+            for (int i = threadIdx.x; i < P; i += kThreads) {
                 const int ixj = i ^ j;
                 if (ixj > i) {
                     const bool asc = (i & k) == 0;
@@ -196,7 +209,7 @@ __device__ inline void bitonic_sort_asc(unsigned long long* key, int P) {
                     }
                 }
             }
-            __syncthreads();
+            csync();
         }
 }
 
@@ -220,12 +233,12 @@ __device__ inline uint32_t block_argmax(const float (&s)[kPer], int base, int cn
             bi = oi;
         }
     }
-    __syncthreads();
+    csync();
     if (lane == 0) {
         sm.redf[warp] = bv;
         sm.redu[warp] = bi;
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
         float v = sm.redf[0];
         uint32_t i = sm.redu[0];
@@ -239,7 +252,7 @@ __device__ inline uint32_t block_argmax(const float (&s)[kPer], int base, int cn
         }
         sm.result = i;
     }
-    __syncthreads();
+    csync();
     return sm.result;
 }
 
@@ -247,7 +260,7 @@ __device__ inline uint32_t block_argmax(const float (&s)[kPer], int base, int cn
 // token.  Returns the token, or 0xffffffff after setting `status` when the
 // reference would throw.  Must be called by all threads of the CTA.
 __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o, uint64_t draw, bool greedy,
-                                       SamplerSmem& sm, float* out_scores, int* status) {
+                                       SamplerSmem& sm, SamplerBig* big, float* out_scores, int* status) {
     const int tid = threadIdx.x;
     const int base = tid * kPer;
     const int cnt = max(0, min(kPer, kVocab - base));
@@ -283,59 +296,80 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
 
     // finite survivors in index order
     uint32_t nf = 0;
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) nf += (k < cnt && isfinite(s[k])) ? 1u : 0u;
-    uint32_t n = 0;
-    uint32_t off = block_excl_scan(nf, sm, &n);
+    float lmax = -INFINITY;
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
         if (k < cnt && isfinite(s[k])) {
-            sm.sv_idx[off] = base + k;
-            sm.sv_s[off] = s[k];
+            ++nf;
+            lmax = fmaxf(lmax, s[k]);
+        }
+    const float mx = cblock_max(lmax, sm.redf);
+    uint32_t n = 0;
+    uint32_t off = block_excl_scan(nf, sm, &n);
+    const bool fast = n <= (uint32_t)kFast;
+    uint32_t* idx = fast ? sm.f_idx : big->sv_idx;
+    float* sc = fast ? sm.f_s : big->sv_s;
+    unsigned long long* key = fast ? sm.f_key : big->key;
+    double* pr = fast ? sm.f_pr : nullptr;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+        if (k < cnt && isfinite(s[k])) {
+            idx[off] = base + k;
+            sc[off] = s[k];
             ++off;
         }
-    for (int i = tid; i < kBits; i += blockDim.x) sm.removed[i] = 0;
-    __syncthreads();
+    for (int i = tid; i < kBits; i += kThreads) sm.removed[i] = 0;
+    csync();
     if (n == 0) {
         if (tid == 0) set_status(status, kStatusNoFiniteLogits, 100, 0);
-        __syncthreads();
+        csync();
         return 0xffffffffu;
+    }
+    // exp(double(s - max)) of every survivor, in parallel (the values the
+    // reference computes one by one; the sums below keep its order)
+    if (pr) {
+        for (uint32_t i = tid; i < n; i += kThreads) pr[i] = exp(double(sc[i] - mx));
+        csync();
     }
 
     if (top_p) {
         int P = 1;
         while (P < (int)n) P <<= 1;
-        for (int i = tid; i < P; i += blockDim.x)
-            sm.key[i] = i < (int)n ? ((unsigned long long)ord_key(sm.sv_s[i]) << 32) | sm.sv_idx[i] : ~0ull;
-        __syncthreads();
-        bitonic_sort_asc(sm.key, P);
+        // (score key, survivor position): position order is index order
+        for (int i = tid; i < P; i += kThreads)
+            key[i] = i < (int)n ? ((unsigned long long)ord_key(sc[i]) << 32) | (uint32_t)i : ~0ull;
+        csync();
+        bitonic_sort_asc(key, P);
         if (tid == 0) {
             sm.err = 0;
-            const float mx = key_float(uint32_t(sm.key[n - 1] >> 32));
             double total = 0.0;
-            for (uint32_t i = 0; i < n; ++i) total += exp(double(sm.sv_s[i] - mx));
+            for (uint32_t i = 0; i < n; ++i) total += pr ? pr[i] : exp(double(sc[i] - mx));
             if (!(total > 0.0)) {
                 sm.err = kStatusZeroMass;
             } else {
                 const double low = 1.0 - double(o.top_p);
                 double cum = 0.0;
                 for (uint32_t j = 0; j < n; ++j) {
-                    const uint32_t idx = uint32_t(sm.key[j]);
-                    const float sc = key_float(uint32_t(sm.key[j] >> 32));
-                    cum += exp(double(sc - mx)) / total;
-                    if (cum <= low) sm.removed[idx >> 5] |= 1u << (idx & 31);
+                    const uint32_t pos = uint32_t(key[j]);
+                    cum += (pr ? pr[pos] : exp(double(sc[pos] - mx))) / total;
+                    if (cum <= low) {
+                        const uint32_t t = idx[pos];
+                        sm.removed[t >> 5] |= 1u << (t & 31);
+                    } else {
+                        break;  // cumulative mass only grows: nothing later is removed
+                    }
                 }
                 const uint32_t keep = (o.num_beams > 1 && n >= 2) ? 2u : 1u;
                 for (uint32_t i = 0; i < keep; ++i) {
-                    const uint32_t idx = uint32_t(sm.key[n - 1 - i]);
-                    sm.removed[idx >> 5] &= ~(1u << (idx & 31));
+                    const uint32_t t = idx[uint32_t(key[n - 1 - i])];
+                    sm.removed[t >> 5] &= ~(1u << (t & 31));
                 }
             }
         }
-        __syncthreads();
+        csync();
         if (sm.err) {
             if (tid == 0) set_status(status, sm.err, 101, 0);
-            __syncthreads();
+            csync();
             return 0xffffffffu;
         }
 #pragma unroll
@@ -350,14 +384,12 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
     }
     if (greedy) return block_argmax(s, base, cnt, sm);
 
-    // CDF sample in index order (thread 0, double precision)
+    // CDF sample in index order (thread 0, double precision).  The maximum is
+    // unchanged by top-p (the top score is always kept).
     if (tid == 0) {
-        float mx = -INFINITY;
-        for (uint32_t i = 0; i < n; ++i)
-            if (!bit_get(sm.removed, sm.sv_idx[i])) mx = fmaxf(mx, sm.sv_s[i]);
         double total = 0.0;
         for (uint32_t i = 0; i < n; ++i)
-            if (!bit_get(sm.removed, sm.sv_idx[i])) total += exp(double(sm.sv_s[i] - mx));
+            if (!bit_get(sm.removed, idx[i])) total += pr ? pr[i] : exp(double(sc[i] - mx));
         if (!(total > 0.0)) {
             set_status(status, kStatusZeroMass, 102, 0);
             sm.result = 0xffffffffu;
@@ -366,21 +398,21 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
             double cum = 0.0;
             uint32_t last = 0, pick = 0xffffffffu;
             for (uint32_t i = 0; i < n; ++i) {
-                const uint32_t idx = sm.sv_idx[i];
-                if (bit_get(sm.removed, idx)) continue;
-                const double p = exp(double(sm.sv_s[i] - mx));
+                const uint32_t t = idx[i];
+                if (bit_get(sm.removed, t)) continue;
+                const double p = pr ? pr[i] : exp(double(sc[i] - mx));
                 if (p <= 0.0) continue;
-                last = idx;
+                last = t;
                 cum += p;
                 if (target < cum) {
-                    pick = idx;
+                    pick = t;
                     break;
                 }
             }
             sm.result = pick == 0xffffffffu ? last : pick;
         }
     }
-    __syncthreads();
+    csync();
     return sm.result;
 }
 
