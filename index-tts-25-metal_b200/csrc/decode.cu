@@ -45,21 +45,6 @@ constexpr int kRowBytes = kWidth * 4;              // every streamed row has 128
 constexpr int kRowsPerSlot = 4;
 constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 20 KB
 constexpr int kSlots = 10;
-constexpr int kPfSlots = 12;
-
-enum Seg : int { kSegLn1 = 0, kSegQkv, kSegO, kSegLn2, kSegFc, kSegMp, kSegFinalLn, kSegHead };
-
-struct Cursor {
-    int step, layer, seg;
-    uint32_t off, budget;
-};
-
-struct SlotDesc {
-    const char* src[4];
-    uint32_t bytes[4];
-    int n;
-    uint32_t total;
-};
 
 struct Ring {
     __align__(128) unsigned char data[kSlots][kSlotBytes];
@@ -88,15 +73,23 @@ __device__ __forceinline__ Rows cta_rows(int cta, int ncta) {
     return r;
 }
 
+constexpr int kMaxRowsPerCta = 64;  // host check: ceil(8194 / grid) <= 64 (so ceil(1280 / grid) <= 16)
+constexpr int kPartStride = 68;     // attention partial: max, sum, 2 pad, 64 outputs
+constexpr int kMaxChunks = 8;       // key chunks per head (partials merged per head)
+
 struct PhaseSmem {
     float red[32];
-    float red2[2][32];
-    float bias[64];
-    float res[64];
-    float f[64];
-    __align__(16) float attn[kWidth];
+    union {
+        float rowred[kMaxRowsPerCta][4];  // 1280-wide rows: sums of the four column quarters
+        float longred[16][kWarps];        // 5120-wide rows: sums of the sixteen warps' columns
+    };
+    float f[kMaxRowsPerCta];          // this CTA's GELU outputs
+    __align__(16) float xin[kWidth];  // residual stream entering the layer (pre-LN1)
+    union {                           // phase B's warp states / phase C's merged heads
+        float wo[kWarps][kHeadDim];
+        __align__(16) float attn[kWidth];
+    };
     float wm[kWarps], wl[kWarps];
-    float wo[kWarps][kHeadDim];
     int abort;
 };
 
@@ -106,6 +99,7 @@ struct DecodeSmem {
     SamplerSmem sa;
     ModelW w;  // the weight pointer table, read at every slot and phase start
 };
+static_assert(sizeof(DecodeSmem) <= 227 * 1024, "decode kernel shared memory above the sm_100 per-CTA limit");
 
 // All threads: copy the weight pointer table into shared memory.
 __device__ __forceinline__ void load_table(ModelW& dst, const ModelW* src) {
@@ -140,9 +134,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 
 // Bounded wait for a ring slot; every thread waits.  The spin touches no
 // global memory for the first kStatusPollNs (a global load costs a full L2
@@ -167,148 +158,125 @@ __device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, int*
     }
 }
 
-__device__ __forceinline__ void advance_seg(Cursor& c, int layers) {
-    if (c.seg == kSegMp) {
-        ++c.layer;
-        c.seg = c.layer == layers ? kSegFinalLn : kSegLn1;
+// The weight schedule of one CTA, as segments of contiguous bytes; segment k
+// of a forward step (6 per layer, then 3 for the head):
+//   6l+0 ln_1 pack           6l+1 its c_attn rows     6l+2 its attn.c_proj rows
+//   6l+3 ln_2 pack           6l+4 its c_fc rows       6l+5 its mlp.c_proj rows (5120 wide)
+//   6L+0 ln_f pack           6L+1 final_norm pack     6L+2 its mel_head rows
+// Segments are cut into 20 KB slots (4 rows of 1280, or one row of 5120).
+__device__ __forceinline__ void seg_of(const ModelW& w, const Rows& r, int k, const char*& p, uint32_t& bytes) {
+    const float* base;
+    int n;  // rows of 1280 floats
+    if (k < 6 * w.layers) {
+        const LayerW& lw = w.layer[k / 6];
+        switch (k % 6) {
+            case 0: base = lw.ln1_pack; n = 2; break;
+            case 1: base = lw.w_qkv + (size_t)r.q0 * kWidth; n = r.q1 - r.q0; break;
+            case 2: base = lw.w_o + (size_t)r.o0 * kWidth; n = r.o1 - r.o0; break;
+            case 3: base = lw.ln2_pack; n = 2; break;
+            case 4: base = lw.w_fc + (size_t)r.f0 * kWidth; n = r.f1 - r.f0; break;
+            default: base = lw.w_mp + (size_t)r.o0 * kFfn; n = (r.o1 - r.o0) * (kFfn / kWidth); break;
+        }
     } else {
-        ++c.seg;
+        const int h = k - 6 * w.layers;
+        if (h == 0) { base = w.head_pack1; n = 2; }
+        else if (h == 1) { base = w.head_pack2; n = 2; }
+        else { base = w.w_head + (size_t)r.h0 * kWidth; n = r.h1 - r.h0; }
     }
+    p = reinterpret_cast<const char*>(base);
+    bytes = uint32_t(n) * kRowBytes;
 }
 
-// The weight schedule of one CTA: per forward step, per layer: LN1 vectors,
-// its QKV rows, its c_proj rows, LN2 vectors, its c_fc rows, its mlp.c_proj
-// [in, out] rows; then the final LN vectors and its mel_head rows.  Row blocks
-// are cut into 4-row slots.
-__device__ bool next_slot(const ModelW& w, const Rows& rows, int n_steps, Cursor& c, SlotDesc& d) {
-    while (c.budget > 0 && c.step < n_steps) {
-        d.n = 0;
-        if (c.seg == kSegLn1 || c.seg == kSegLn2) {
-            const LayerW& lw = w.layer[c.layer];
-            d.src[0] = reinterpret_cast<const char*>(c.seg == kSegLn1 ? lw.ln1_g : lw.ln2_g);
-            d.src[1] = reinterpret_cast<const char*>(c.seg == kSegLn1 ? lw.ln1_b : lw.ln2_b);
-            d.bytes[0] = d.bytes[1] = kRowBytes;
-            d.n = 2;
-            d.total = 2 * kRowBytes;
-            advance_seg(c, w.layers);
-            --c.budget;
-            return true;
-        }
-        if (c.seg == kSegFinalLn) {
-            const float* v[4] = {w.lnf_g, w.lnf_b, w.fn_g, w.fn_b};
-            for (int i = 0; i < 4; ++i) {
-                d.src[i] = reinterpret_cast<const char*>(v[i]);
-                d.bytes[i] = kRowBytes;
-            }
-            d.n = 4;
-            d.total = 4 * kRowBytes;
-            c.seg = kSegHead;
-            --c.budget;
-            return true;
-        }
-        const float* base;
-        int r0, r1;
-        if (c.seg == kSegHead) {
-            base = w.w_head;
-            r0 = rows.h0;
-            r1 = rows.h1;
-        } else {
-            const LayerW& lw = w.layer[c.layer];
-            if (c.seg == kSegQkv) {
-                base = lw.w_qkv;
-                r0 = rows.q0;
-                r1 = rows.q1;
-            } else if (c.seg == kSegO) {
-                base = lw.w_o;
-                r0 = rows.o0;
-                r1 = rows.o1;
-            } else {
-                base = c.seg == kSegFc ? lw.w_fc : lw.w_mpT;
-                r0 = rows.f0;
-                r1 = rows.f1;
-            }
-        }
-        const uint32_t total = uint32_t(r1 - r0) * kRowBytes;
-        if (c.off < total) {
-            const uint32_t chunk = min(total - c.off, (uint32_t)kSlotBytes);
-            d.src[0] = reinterpret_cast<const char*>(base + (size_t)r0 * kWidth) + c.off;
-            d.bytes[0] = chunk;
-            d.n = 1;
-            d.total = chunk;
-            c.off += chunk;
-            if (c.off >= total) {
-                c.off = 0;
-                if (c.seg == kSegHead) {
-                    ++c.step;
-                    c.layer = 0;
-                    c.seg = kSegLn1;
-                } else {
-                    advance_seg(c, w.layers);
-                }
-            }
-            --c.budget;
-            return true;
-        }
+__device__ __forceinline__ int segs_per_step(const ModelW& w) { return 6 * w.layers + 3; }
+
+// Schedule position of the L2 prefetch that runs ahead of the ring.
+struct PfCursor {
+    int step, k;
+    uint32_t off, seg_bytes;
+    unsigned long long pos;  // schedule bytes passed so far
+    const char* p;
+};
+
+constexpr uint32_t kPfChunk = 32768;
+constexpr unsigned long long kPfAhead = 256ull * 1024;  // bytes of schedule kept in flight beyond the ring
+
+// Moves the prefetch cursor by one chunk (issuing cp.async.bulk.prefetch.L2
+// for it when `issue`); false at the end of the schedule.
+__device__ __forceinline__ bool pf_advance(const ModelW& w, const Rows& rows, int k0, int k1, int n_steps,
+                                           PfCursor& c, bool issue) {
+    while (c.off >= c.seg_bytes) {  // next non-empty segment
         c.off = 0;
-        if (c.seg == kSegHead) {
-            ++c.step;
-            c.layer = 0;
-            c.seg = kSegLn1;
-        } else {
-            advance_seg(c, w.layers);
+        if (++c.k >= k1) {
+            c.k = k0;
+            if (++c.step >= n_steps) return false;
         }
+        seg_of(w, rows, c.k, c.p, c.seg_bytes);
     }
-    return false;
+    const uint32_t n = min(c.seg_bytes - c.off, kPfChunk);
+    if (issue) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c.p + c.off), "r"(n) : "memory");
+    c.off += n;
+    c.pos += n;
+    return true;
 }
 
-// Producer warp (lane 0): walks the schedule, waits for a slot's previous use
-// to be handed back, and issues its bulk copies.  While it waits on a full
-// ring (the consumers are in a grid barrier, the attention phase or the
-// sampler) it prefetches up to kPfSlots further slots into L2, so HBM keeps
-// streaming; continuous prefetching slows the steady stream, so it is not done
-// otherwise.  Every wait is bounded and also ends when the consumers raise
-// `stop`.
-__device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Rows& rows, Cursor start, int n_steps) {
+// Bounded wait of the producer for a slot's previous use to be handed back;
+// while it waits it keeps the L2 prefetch kPfAhead bytes ahead of the ring.
+// False when the consumers raised `stop`, on an error status or on timeout.
+__device__ bool wait_empty(Ring& R, int s, uint32_t parity, int* status, uint32_t j, const ModelW& w,
+                           const Rows& rows, int k0, int k1, int n_steps, PfCursor& pf, unsigned long long issued) {
+    if (mbar_try_wait(&R.empty[s], parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    bool more = true;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(&R.empty[s], parity)) return true;
+        if (more && pf.pos < issued + kPfAhead) {
+            more = pf_advance(w, rows, k0, k1, n_steps, pf, pf.pos >= issued);
+            continue;
+        }
+        if ((i & 63u) == 0) {
+            if (R.stop) return false;
+            const unsigned long long dt = globaltimer_ns() - t0;
+            if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
+            if (dt > kWaitLimitNs) {
+                set_status(status, kStatusRingTimeout, 900, (int)j);
+                return false;
+            }
+        }
+    }
+}
+
+// Producer warp (lane 0): issues segments [k0, k1) of each of n_steps forward
+// steps into the ring, one bulk copy per slot, waiting for a slot's previous
+// use to be handed back before reusing it.
+__device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Rows& rows, int k0, int k1, int n_steps) {
     int* status = a.b.ctl->status;
-    Cursor tma = start, pf = start;
-    SlotDesc d, dp;
-    uint32_t j = 0, pfn = 0;  // slots issued; slots the prefetch cursor has passed
-    while (!R.stop && next_slot(w, rows, n_steps, tma, d)) {
-        const int s = j % kSlots;
-        if (j >= kSlots) {
-            const uint32_t parity = ((j / kSlots) - 1) & 1u;
-            const unsigned long long t0 = globaltimer_ns();
-            bool ok = true;
-            for (uint32_t i = 0; !mbar_try_wait(&R.empty[s], parity); ++i) {
-                if (pfn < j + 1 + kPfSlots && next_slot(w, rows, n_steps, pf, dp)) {
-                    if (pfn > j)  // slots up to j are already issued or being issued
-                        for (int q = 0; q < dp.n; ++q) bulk_prefetch_l2(dp.src[q], dp.bytes[q]);
-                    ++pfn;
-                    continue;
-                }
-                if ((i & 63u) == 63u) {
-                    if (R.stop) { ok = false; break; }
-                    const unsigned long long dt = globaltimer_ns() - t0;
-                    if (dt > kStatusPollNs && ld_volatile(status) != 0) { ok = false; break; }
-                    if (dt > kWaitLimitNs) {
-                        set_status(status, kStatusRingTimeout, 900, (int)j);
-                        ok = false;
-                        break;
-                    }
+    uint32_t j = 0, parity = 0;
+    int s = 0;
+    unsigned long long issued = 0;  // schedule bytes issued into the ring
+    PfCursor pf{0, k0 - 1, 0, 0, 0, nullptr};
+    for (int step = 0; step < n_steps; ++step) {
+        for (int k = k0; k < k1; ++k) {
+            const char* p;
+            uint32_t bytes;
+            seg_of(w, rows, k, p, bytes);
+            for (uint32_t off = 0; off < bytes; off += kSlotBytes) {
+                const uint32_t n = min(bytes - off, (uint32_t)kSlotBytes);
+                if (j >= kSlots &&
+                    !wait_empty(R, s, parity ^ 1u, status, j, w, rows, k0, k1, n_steps, pf, issued))
+                    goto done;
+                mbar_expect_tx(&R.full[s], n);
+                bulk_g2s(R.data[s], p + off, n, &R.full[s]);
+                issued += n;
+                ++j;
+                R.issued = j;
+                if (++s == kSlots) {
+                    s = 0;
+                    parity ^= 1u;
                 }
             }
-            if (!ok) break;
         }
-        mbar_expect_tx(&R.full[s], d.total);
-        unsigned char* dst = R.data[s];
-        for (int i = 0; i < d.n; ++i) {
-            bulk_g2s(dst, d.src[i], d.bytes[i], &R.full[s]);
-            dst += d.bytes[i];
-        }
-        ++j;
-        R.issued = j;
-        while (pfn < j && next_slot(w, rows, n_steps, pf, dp)) ++pfn;  // keep the prefetch cursor ahead
     }
+done:
     __threadfence_block();
     R.producer_done = 1;
 }
@@ -333,7 +301,7 @@ __device__ void ring_finish(Ring& R, uint32_t consumed) {
 __device__ void ring_init(Ring& R) {
     for (int i = 0; i < kSlots; ++i) {
         mbar_init(&R.full[i], 1);
-        mbar_init(&R.empty[i], 1);
+        mbar_init(&R.empty[i], kWarps);
     }
     R.issued = 0;
     R.stop = 0;
@@ -348,20 +316,24 @@ struct Ctx {
     PhaseSmem& sm;
     Rows rows;
     int cta, ncta;
-    uint32_t k;  // slots consumed so far (uniform across the consumers)
+    uint32_t k;       // slots consumed so far (uniform across the consumers)
+    bool resident;    // persistent kernel: sm.xin survives from phase A to phase C
 };
 
-// Every consumer thread waits for the next slot.  The caller folds `ok` into
-// its next csync_or so that an abort is taken uniformly.
+// Every consumer thread waits for the next slot; `ok` is warp-uniform.
 __device__ __forceinline__ const float* slot_wait(Ctx& cx, bool& ok, int where) {
     const int s = cx.k % kSlots;
     ok = mbar_wait_bounded(&cx.R.full[s], (cx.k / kSlots) & 1u, cx.a.b.ctl->status, where);
+    ok = __all_sync(0xffffffffu, ok);
     return reinterpret_cast<const float*>(cx.R.data[s]);
 }
 
-// After a csync that follows the last read of the slot: hand it back.
+// After this warp's last read of the slot: lane 0 hands the warp's share back
+// (the empty barrier completes when all 16 consumer warps have arrived, so
+// warps run through the ring independently of one another).
 __device__ __forceinline__ void slot_release(Ctx& cx) {
-    if (threadIdx.x == 0) mbar_arrive(&cx.R.empty[cx.k % kSlots]);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&cx.R.empty[cx.k % kSlots]);
     ++cx.k;
 }
 
@@ -400,93 +372,124 @@ __device__ void layernorm2(float2 (&x)[5], const float* g, const float* b, float
     }
 }
 
-// Consumes the slot holding LayerNorm vectors and normalises x with the first
-// (and, for the head, the second) pair.
-__device__ bool ln_slot(Ctx& cx, float2 (&x)[5], int pairs, int where) {
+// Waits for the slot holding LayerNorm vectors (an abort is taken uniformly).
+__device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool& abort, int where) {
     bool ok;
     const float* slot = slot_wait(cx, ok, where);
-    if (csync_or(!ok)) return false;
-    layernorm2(x, slot, slot + kWidth, cx.sm.red);
-    if (pairs == 2) layernorm2(x, slot + 2 * kWidth, slot + 3 * kWidth, cx.sm.red);
-    csync();
-    slot_release(cx);
-    return true;
+    abort = csync_or(!ok);
+    return slot;
 }
 
-// y[row] = W[row, :] . x for `nrows` streamed rows (4 per slot); epi(row, y)
-// runs on consumer thread `row` after the slot's reduction.
+// y[row] = W[row, :] . x for `nrows` streamed rows (4 per slot).  Warp w takes
+// row w/4 of each slot and column quarter w%4; the quarter sums stay in shared
+// memory and are added once, after the last slot, when epi(row, y) runs on
+// consumer thread `row`.  No CTA-wide barrier inside the loop.
 template <class Epi>
 __device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[5], int where, Epi epi) {
-    const int t = threadIdx.x, rr = t >> 7, tig = t & 127, warp = t >> 5, lane = t & 31;
-    for (int r0 = 0; r0 < nrows; r0 += kRowsPerSlot) {
-        bool ok;
+    const int t = threadIdx.x, rr = t >> 7, q = (t >> 5) & 3, tig = t & 127, lane = t & 31;
+    bool ok = true;
+    for (int r0 = 0; r0 < nrows && ok; r0 += kRowsPerSlot) {
         const float* slot = slot_wait(cx, ok, where);
-        float acc = 0.f;
-        if (ok && r0 + rr < nrows) {
+        if (!ok) break;
+        if (r0 + rr < nrows) {
             const float2* w = reinterpret_cast<const float2*>(slot + rr * kWidth) + tig;
+            float acc = 0.f;
 #pragma unroll
             for (int j = 0; j < 5; ++j) {
                 const float2 wv = w[j * 128];
                 acc = fmaf(wv.x, x[j].x, acc);
                 acc = fmaf(wv.y, x[j].y, acc);
             }
+            acc = warp_sum(acc);
+            if (lane == 0) cx.sm.rowred[r0 + rr][q] = acc;
         }
-        acc = warp_sum(acc);
-        float* rb = cx.sm.red2[cx.k & 1];
-        if (lane == 0) rb[warp] = acc;
-        if (csync_or(!ok)) return false;
         slot_release(cx);
-        if (t < kRowsPerSlot && r0 + t < nrows) epi(r0 + t, (rb[4 * t] + rb[4 * t + 1]) + (rb[4 * t + 2] + rb[4 * t + 3]));
+    }
+    if (csync_or(!ok)) return false;
+    if (t < nrows) {
+        const float* s = cx.sm.rowred[t];
+        epi(t, (s[0] + s[1]) + (s[2] + s[3]));
     }
     return true;
 }
 
-constexpr float kFixScale = 4294967296.0f;  // 2^32
-constexpr double kFixInv = 1.0 / 4294967296.0;
-
-// Row r of the residual stream entering in-step layer `li` (li = layers: the
-// input of the head).  li = 0: the token embedding (gpt_build_current,
-// kernels.metal:1310-1325); otherwise r + (mlp.c_proj output + bias) of the
-// previous layer, the output being the fixed-point sum of the CTAs' shares.
-__device__ __forceinline__ float resid_in(const DecodeArgs& a, const ModelW& w, int li, int g, uint32_t token,
-                                         uint32_t pos, int r) {
-    if (li == 0)
-        return __ldg(w.mel_emb + (size_t)token * kWidth + r) + __ldg(w.mel_pos + (size_t)pos * kWidth + r);
-    const int gp = (g - 1) & 1;
-    const float mp = float(double(__ldcg(a.b.acc + gp * kWidth + r)) * kFixInv);
-    return __ldcg(a.b.r + gp * kWidth + r) + (mp + __ldg(w.layer[li - 1].b_mp + r));
-}
-
-__device__ __forceinline__ void load_resid(const DecodeArgs& a, const ModelW& w, int li, int g, uint32_t token,
-                                           uint32_t pos, float2 (&x)[5]) {
-    if (a.head_src && li == w.layers) {  // prefill: the last hidden row
-#pragma unroll
-        for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.head_src + col_of(j)));
-        return;
-    }
+// The residual stream entering in-step layer `li` (li = layers: the input of
+// the head), in x's layout: li = 0 the token embedding (gpt_build_current,
+// kernels.metal:1310-1325), otherwise the previous layer's output h.
+__device__ __forceinline__ void load_resid(const DecodeArgs& a, const ModelW& w, int li, uint32_t token, uint32_t pos,
+                                           float2 (&x)[5]) {
 #pragma unroll
     for (int j = 0; j < 5; ++j) {
         const int c = col_of(j);
-        x[j] = make_float2(resid_in(a, w, li, g, token, pos, c), resid_in(a, w, li, g, token, pos, c + 1));
+        if (a.head_src && li == w.layers) {  // prefill: the last hidden row
+            x[j] = __ldcg(reinterpret_cast<const float2*>(a.head_src + c));
+        } else if (li == 0) {
+            const float2 e = __ldg(reinterpret_cast<const float2*>(w.mel_emb + (size_t)token * kWidth + c));
+            const float2 p = __ldg(reinterpret_cast<const float2*>(w.mel_pos + (size_t)pos * kWidth + c));
+            x[j] = make_float2(e.x + p.x, e.y + p.y);
+        } else {
+            x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.h + c));
+        }
     }
 }
 
-// ---------------------------------------------------------------- phases
-__device__ bool phase_qkv(Ctx& cx, int li, int g, uint32_t token, uint32_t pos) {
-    const DecodeArgs& a = cx.a;
-    const LayerW& L = cx.w.layer[li];
-    const int r0 = cx.rows.q0, r1 = cx.rows.q1;
-    if ((int)threadIdx.x < r1 - r0) cx.sm.bias[threadIdx.x] = __ldg(L.b_qkv + r0 + threadIdx.x);
-    float2 x[5];
-    load_resid(a, cx.w, li, g, token, pos, x);
-    if (!ln_slot(cx, x, 1, 10 + li)) return false;
-    float* out = a.b.qkv + r0;
-    const float* bias = cx.sm.bias;
-    return gemv_slots(cx, r1 - r0, x, 40 + li, [&](int row, float v) { out[row] = v + bias[row]; });
+// y[row] = W[row, :] . f for `nrows` streamed 5120-wide rows (one per slot);
+// thread t owns columns 2t + 1024j (+1), j < 5, of f.  The sixteen warp sums of
+// a row are added once, after the last slot, when epi(row, y) runs on thread `row`.
+template <class Epi>
+__device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[5], int where, Epi epi) {
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    bool ok = true;
+    for (int r = 0; r < nrows && ok; ++r) {
+        const float* slot = slot_wait(cx, ok, where);
+        if (!ok) break;
+        const float2* w = reinterpret_cast<const float2*>(slot) + t;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const float2 wv = w[j * kThreads];
+            acc = fmaf(wv.x, x[j].x, acc);
+            acc = fmaf(wv.y, x[j].y, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) cx.sm.longred[r][warp] = acc;
+        slot_release(cx);
+    }
+    if (csync_or(!ok)) return false;
+    if (t < nrows) {
+        const float* s = cx.sm.longred[t];
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = s[2 * i] + s[2 * i + 1];
+        epi(t, ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7])));
+    }
+    return true;
 }
 
+// ---------------------------------------------------------------- phases
+__device__ bool phase_qkv(Ctx& cx, int li, uint32_t token, uint32_t pos) {
+    const DecodeArgs& a = cx.a;
+    const int t = threadIdx.x, r0 = cx.rows.q0, nrows = cx.rows.q1 - r0;
+    const float bias = t < nrows ? __ldg(cx.w.layer[li].b_qkv + r0 + t) : 0.f;  // used after the last slot
+    float2 x[5];
+    load_resid(a, cx.w, li, token, pos, x);
+    bool abort;
+    const float* slot = ln_slot_wait(cx, abort, 10 + li);
+    if (abort) return false;
+    if (t < 128)
+#pragma unroll
+        for (int j = 0; j < 5; ++j) *reinterpret_cast<float2*>(&cx.sm.xin[col_of(j)]) = x[j];
+    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    slot_release(cx);
+    float* out = a.b.qkv + r0;
+    return gemv_slots(cx, nrows, x, 40 + li, [&](int row, float v) { out[row] = v + bias; });
+}
+
+// Key chunk of one attention unit: a multiple of 16 keys, at most kMaxChunks
+// chunks per head, about one unit per CTA.
 __device__ __forceinline__ uint32_t attn_chunk(uint32_t keys, int ncta) {
     uint32_t ch = (keys * kHeads + ncta - 1) / ncta;
+    ch = max(ch, (keys + kMaxChunks - 1) / kMaxChunks);
     return max((ch + 15u) & ~15u, 16u);
 }
 
@@ -569,8 +572,8 @@ __device__ void phase_attn(Ctx& cx, int li, uint32_t S) {
                 Ls = fmaf(e, cx.sm.wl[w], Ls);
                 O = fmaf(e, cx.sm.wo[w][t], O);
             }
-            float* pp = a.b.part + ((size_t)h * nch + c) * 66;
-            pp[2 + t] = O;
+            float* pp = a.b.part + ((size_t)h * nch + c) * kPartStride;
+            pp[4 + t] = O;
             if (t == 0) {
                 pp[0] = M;
                 pp[1] = Ls;
@@ -586,102 +589,112 @@ __device__ void phase_attn(Ctx& cx, int li, uint32_t S) {
     }
 }
 
-__device__ bool phase_oproj(Ctx& cx, int li, int g, uint32_t token, uint32_t pos, uint32_t S) {
+__device__ bool phase_oproj(Ctx& cx, int li, uint32_t token, uint32_t pos, uint32_t S) {
     const DecodeArgs& a = cx.a;
-    const LayerW& L = cx.w.layer[li];
-    const int r0 = cx.rows.o0, r1 = cx.rows.o1;
+    const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0;
     const int t = threadIdx.x;
-    if (t < r1 - r0) {
-        cx.sm.bias[t] = __ldg(L.b_o + r0 + t);
-        cx.sm.res[t] = resid_in(a, cx.w, li, g, token, pos, r0 + t);
+    float bias = 0.f, res = 0.f;  // used after the last slot
+    if (t < nrows) {
+        const int r = r0 + t;
+        bias = __ldg(cx.w.layer[li].b_o + r);
+        if (cx.resident)
+            res = cx.sm.xin[r];
+        else if (li == 0)  // layered path: the layer input from global memory
+            res = __ldg(cx.w.mel_emb + (size_t)token * kWidth + r) + __ldg(cx.w.mel_pos + (size_t)pos * kWidth + r);
+        else
+            res = __ldcg(a.b.h + r);
     }
-    // merge the split-K attention partials of every head (same chunking as B)
+    // merge the split-K attention partials: warp w merges heads w and w + 16,
+    // lane l outputs 2l, 2l+1; all loads of a head's partials are in flight together
     const uint32_t keys = S + 1;
     const uint32_t ch = attn_chunk(keys, cx.ncta);
-    const uint32_t nch = (keys + ch - 1) / ch;
-    if (t < kWidth / 4) {
-        const int h = (4 * t) / kHeadDim, d = (4 * t) % kHeadDim;
-        const float* ph = a.b.part + (size_t)h * nch * 66;
-        float M = -INFINITY;
-        for (uint32_t c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(ph + c * 66));
-        float Ls = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        for (uint32_t c = 0; c < nch; ++c) {
-            const float* pc = ph + c * 66;
-            const float e = expf(__ldcg(pc) - M);
-            Ls = fmaf(e, __ldcg(pc + 1), Ls);
-            o0 = fmaf(e, __ldcg(pc + 2 + d), o0);
-            o1 = fmaf(e, __ldcg(pc + 3 + d), o1);
-            o2 = fmaf(e, __ldcg(pc + 4 + d), o2);
-            o3 = fmaf(e, __ldcg(pc + 5 + d), o3);
+    const int nch = int((keys + ch - 1) / ch);
+    const int lane = t & 31;
+    for (int h = t >> 5; h < kHeads; h += kWarps) {
+        const float* ph = a.b.part + (size_t)h * nch * kPartStride;
+        float2 ml[kMaxChunks], ov[kMaxChunks];
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+            if (c < nch) {
+                ml[c] = __ldcg(reinterpret_cast<const float2*>(ph + c * kPartStride));
+                ov[c] = __ldcg(reinterpret_cast<const float2*>(ph + c * kPartStride + 4) + lane);
+            }
         }
-        *reinterpret_cast<float4*>(&cx.sm.attn[4 * t]) = make_float4(o0 / Ls, o1 / Ls, o2 / Ls, o3 / Ls);
+        float M = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c)
+            if (c < nch) M = fmaxf(M, ml[c].x);
+        float Ls = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < kMaxChunks; ++c) {
+            if (c < nch) {
+                const float e = expf(ml[c].x - M);
+                Ls = fmaf(e, ml[c].y, Ls);
+                o0 = fmaf(e, ov[c].x, o0);
+                o1 = fmaf(e, ov[c].y, o1);
+            }
+        }
+        *reinterpret_cast<float2*>(&cx.sm.attn[h * kHeadDim + 2 * lane]) = make_float2(o0 / Ls, o1 / Ls);
     }
     csync();
     float2 x[5];
 #pragma unroll
     for (int j = 0; j < 5; ++j) x[j] = *reinterpret_cast<const float2*>(&cx.sm.attn[col_of(j)]);
-    float* out = a.b.r + (g & 1) * kWidth + r0;
-    const float* bias = cx.sm.bias;
-    const float* res = cx.sm.res;
-    return gemv_slots(cx, r1 - r0, x, 70 + li, [&](int row, float v) { out[row] = res[row] + (v + bias[row]); });
+    float* out = a.b.hm + r0;
+    return gemv_slots(cx, nrows, x, 70 + li, [&](int row, float v) { out[row] = res + (v + bias); });
 }
 
-__device__ bool phase_mlp(Ctx& cx, int li, int g) {
+// hm -> LN2 -> this CTA's c_fc rows -> GELU -> f.
+__device__ bool phase_fc(Ctx& cx, int li) {
     const DecodeArgs& a = cx.a;
-    const LayerW& L = cx.w.layer[li];
-    const int f0 = cx.rows.f0, f1 = cx.rows.f1;
-    const int nf = f1 - f0, t = threadIdx.x;
-    if (t < nf) cx.sm.bias[t] = __ldg(L.b_fc + f0 + t);
-    // clear this CTA's share of the accumulator the next layer will use
-    if (t < cx.rows.o1 - cx.rows.o0) a.b.acc[((g + 1) & 1) * kWidth + cx.rows.o0 + t] = 0ll;
+    const int f0 = cx.rows.f0, nf = cx.rows.f1 - f0, t = threadIdx.x;
+    const float bias = t < nf ? __ldg(cx.w.layer[li].b_fc + f0 + t) : 0.f;
     float2 x[5];
 #pragma unroll
-    for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.r + (g & 1) * kWidth + col_of(j)));
-    if (!ln_slot(cx, x, 1, 100 + li)) return false;
-    float* f = cx.sm.f;
-    const float* bias = cx.sm.bias;
-    if (!gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { f[row] = gelu_ref(v + bias[row]); })) return false;
-    csync();
-    // split-K share of mlp.c_proj: out[j] += sum_{i in rows} WT[i, j] * f[i]
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r0 = 0; r0 < nf; r0 += kRowsPerSlot) {
-        bool ok;
-        const float* slot = slot_wait(cx, ok, 160 + li);
-        if (ok && t < kWidth / 4) {
-            const int n = min(kRowsPerSlot, nf - r0);
-            for (int rr = 0; rr < n; ++rr) {
-                const float4 w = reinterpret_cast<const float4*>(slot + rr * kWidth)[t];
-                const float fv = f[r0 + rr];
-                acc.x = fmaf(w.x, fv, acc.x);
-                acc.y = fmaf(w.y, fv, acc.y);
-                acc.z = fmaf(w.z, fv, acc.z);
-                acc.w = fmaf(w.w, fv, acc.w);
-            }
-        }
-        if (csync_or(!ok)) return false;
-        slot_release(cx);
+    for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.hm + col_of(j)));
+    bool abort;
+    const float* slot = ln_slot_wait(cx, abort, 100 + li);
+    if (abort) return false;
+    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    slot_release(cx);
+    float* out = a.b.f + f0;
+    return gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); });
+}
+
+// f -> this CTA's mlp.c_proj rows (the rows of its attn.c_proj block) -> h = hm + y + bias.
+__device__ bool phase_mp(Ctx& cx, int li) {
+    const DecodeArgs& a = cx.a;
+    const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0, t = threadIdx.x;
+    float bias = 0.f, res = 0.f;
+    if (t < nrows) {
+        bias = __ldg(cx.w.layer[li].b_mp + r0 + t);
+        res = __ldcg(a.b.hm + r0 + t);
     }
-    if (t < kWidth / 4) {
-        unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.b.acc + (g & 1) * kWidth) + 4 * t;
-        atomicAdd(dst + 0, (unsigned long long)__float2ll_rn(acc.x * kFixScale));
-        atomicAdd(dst + 1, (unsigned long long)__float2ll_rn(acc.y * kFixScale));
-        atomicAdd(dst + 2, (unsigned long long)__float2ll_rn(acc.z * kFixScale));
-        atomicAdd(dst + 3, (unsigned long long)__float2ll_rn(acc.w * kFixScale));
-    }
-    return true;
+    float2 x[5];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.f) + t + j * kThreads);
+    float* out = a.b.h + r0;
+    return gemv_long_slots(cx, nrows, x, 160 + li, [&](int row, float v) { out[row] = res + (v + bias); });
 }
 
 // gpt.cpp:120-122: last hidden row -> ln_f -> final_norm -> mel_head.
-__device__ bool phase_head(Ctx& cx, int g, uint32_t token, uint32_t pos) {
+__device__ bool phase_head(Ctx& cx, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
-    const int r0 = cx.rows.h0, r1 = cx.rows.h1;
-    if ((int)threadIdx.x < r1 - r0) cx.sm.bias[threadIdx.x] = __ldg(cx.w.b_head + r0 + threadIdx.x);
+    const int t = threadIdx.x, r0 = cx.rows.h0, nrows = cx.rows.h1 - r0;
+    const float bias = t < nrows ? __ldg(cx.w.b_head + r0 + t) : 0.f;
     float2 x[5];
-    load_resid(a, cx.w, cx.w.layers, g, token, pos, x);
-    if (!ln_slot(cx, x, 2, 200)) return false;
+    load_resid(a, cx.w, cx.w.layers, token, pos, x);
+    bool abort;
+    const float* slot = ln_slot_wait(cx, abort, 200);
+    if (abort) return false;
+    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    slot_release(cx);
+    slot = ln_slot_wait(cx, abort, 200);
+    if (abort) return false;
+    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    slot_release(cx);
     float* out = a.b.logits + r0;
-    const float* bias = cx.sm.bias;
-    return gemv_slots(cx, r1 - r0, x, 201, [&](int row, float v) { out[row] = v + bias[row]; });
+    return gemv_slots(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
 }
 
 // Grid barrier of the persistent kernel (all CTAs co-resident by the
@@ -714,18 +727,25 @@ __device__ bool grid_barrier(Ctx& cx, unsigned& target, int where) {
     return cx.sm.abort != 0;
 }
 
-// One forward step; true when aborted.
-__device__ bool forward_step(Ctx& cx, int step, uint32_t token, uint32_t pos, uint32_t S, unsigned& target) {
+// One forward step; true when aborted.  Five grid barriers per layer: after
+// the QKV rows, the attention partials, the residual after attention, the
+// GELU outputs and the layer output.
+__device__ bool forward_step(Ctx& cx, uint32_t token, uint32_t pos, uint32_t S, unsigned& target) {
     const int L = cx.w.layers;
     for (int li = 0; li < L; ++li) {
-        const int g = step * L + li;
-        if (!phase_qkv(cx, li, g, token, pos) || grid_barrier(cx, target, li * 8 + 0)) return true;
+        if (!phase_qkv(cx, li, token, pos) || grid_barrier(cx, target, li * 8 + 0)) return true;
         phase_attn(cx, li, S);
         if (grid_barrier(cx, target, li * 8 + 1)) return true;
-        if (!phase_oproj(cx, li, g, token, pos, S) || grid_barrier(cx, target, li * 8 + 2)) return true;
-        if (!phase_mlp(cx, li, g) || grid_barrier(cx, target, li * 8 + 3)) return true;
+        if (!phase_oproj(cx, li, token, pos, S) || grid_barrier(cx, target, li * 8 + 2)) return true;
+        if (!phase_fc(cx, li) || grid_barrier(cx, target, li * 8 + 3)) return true;
+        if (!phase_mp(cx, li) || grid_barrier(cx, target, li * 8 + 4)) return true;
     }
-    return !phase_head(cx, step * L + L, token, pos) || grid_barrier(cx, target, 1000);
+    return !phase_head(cx, token, pos) || grid_barrier(cx, target, 1000);
+}
+
+// The sampler in its own frame, so its registers do not constrain the phases.
+__device__ __noinline__ uint32_t sample_next(const DecodeArgs& a, uint32_t i, SamplerSmem& sa, SamplerBig* big) {
+    return run_sampler(a.b.logits, a.opts, i, a.opts.do_sample == 0, sa, big, nullptr, a.b.ctl->status);
 }
 
 constexpr int kCtaThreads = kThreads + 32;  // 16 consumer warps + the producer warp
@@ -744,19 +764,19 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
     __syncthreads();
     if (threadIdx.x >= kThreads) {  // producer warp
         if (threadIdx.x == kThreads) {
-            if (n_fwd > 0) producer(a, sm.w, sm.ring, rows, Cursor{0, 0, kSegLn1, 0, 0xffffffffu}, n_fwd);
+            if (n_fwd > 0) producer(a, sm.w, sm.ring, rows, 0, segs_per_step(sm.w), n_fwd);
             else sm.ring.producer_done = 1;
         }
         return;
     }
     sampler_init_seen(sm.sa, a.history, a.history_n);
-    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0};
+    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, true};
     SamplerBig* big = a.b.sampler_big + cta;
     unsigned target = 0;
     uint32_t token = a.first_code, n_codes = 0, stopped = 0, fwd = 0;
     for (uint32_t i = 0; i < a.n_iter; ++i) {
         if (a.mode == kModeGenerate) {
-            token = run_sampler(a.b.logits, a.opts, i, a.opts.do_sample == 0, sm.sa, big, nullptr, a.b.ctl->status);
+            token = sample_next(a, i, sm.sa, big);
             if (token == (uint32_t)kStopCode) {
                 stopped = 1;
                 break;
@@ -771,7 +791,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
             sampler_mark_seen(sm.sa, token);
             if (i + 1 == a.n_iter) break;
         }
-        if (forward_step(cx, int(i), token, a.pos0 + i, a.s0 + i, target)) break;
+        if (forward_step(cx, token, a.pos0 + i, a.s0 + i, target)) break;
         ++fwd;
     }
     if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
@@ -787,9 +807,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
 }
 
 // ------------------------------------------------------------ layered path
-enum LayerPhase : int { kPhQkv = 0, kPhAttn, kPhOproj, kPhMlp, kPhHead };
+enum LayerPhase : int { kPhQkv = 0, kPhAttn, kPhOproj, kPhFc, kPhMp, kPhHead };
 
-__global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phase, int li, int g, uint32_t pos,
+__global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phase, int li, uint32_t pos,
                                                           uint32_t S) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
@@ -801,34 +821,27 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phas
     __syncthreads();
     if (threadIdx.x >= kThreads) {  // producer warp: exactly this phase's slots
         if (threadIdx.x == kThreads) {
-            Cursor c{0, li, kSegLn1, 0, 0};
-            const int nq = rows.q1 - rows.q0, no = rows.o1 - rows.o0, nf = rows.f1 - rows.f0, nh = rows.h1 - rows.h0;
-            if (phase == kPhQkv) {
-                c.budget = 1 + (nq + kRowsPerSlot - 1) / kRowsPerSlot;
-            } else if (phase == kPhOproj) {
-                c.seg = kSegO;
-                c.budget = (no + kRowsPerSlot - 1) / kRowsPerSlot;
-            } else if (phase == kPhMlp) {
-                c.seg = kSegLn2;
-                c.budget = 1 + 2 * ((nf + kRowsPerSlot - 1) / kRowsPerSlot);
-            } else if (phase == kPhHead) {
-                c.layer = sm.w.layers;
-                c.seg = kSegFinalLn;
-                c.budget = 1 + (nh + kRowsPerSlot - 1) / kRowsPerSlot;
-            }
-            if (c.budget) producer(a, sm.w, sm.ring, rows, c, 1);
+            // segments of this phase (see seg_of)
+            int k0 = 6 * li, k1 = 6 * li;
+            if (phase == kPhQkv) k1 = k0 + 2;
+            else if (phase == kPhOproj) k0 += 2, k1 = k0 + 1;
+            else if (phase == kPhFc) k0 += 3, k1 = k0 + 2;
+            else if (phase == kPhMp) k0 += 5, k1 = k0 + 1;
+            else if (phase == kPhHead) k0 = 6 * sm.w.layers, k1 = k0 + 3;
+            if (k1 > k0) producer(a, sm.w, sm.ring, rows, k0, k1, 1);
             else sm.ring.producer_done = 1;
         }
         return;
     }
     const uint32_t token = *reinterpret_cast<volatile uint32_t*>(&a.b.ctl->token);
-    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0};
+    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, false};
     switch (phase) {
-        case kPhQkv: phase_qkv(cx, li, g, token, pos); break;
+        case kPhQkv: phase_qkv(cx, li, token, pos); break;
         case kPhAttn: phase_attn(cx, li, S); break;
-        case kPhOproj: phase_oproj(cx, li, g, token, pos, S); break;
-        case kPhMlp: phase_mlp(cx, li, g); break;
-        default: phase_head(cx, g, token, pos); break;
+        case kPhOproj: phase_oproj(cx, li, token, pos, S); break;
+        case kPhFc: phase_fc(cx, li); break;
+        case kPhMp: phase_mp(cx, li); break;
+        default: phase_head(cx, token, pos); break;
     }
     if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
 }
@@ -967,13 +980,12 @@ cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cud
         if (a.mode == kModeGenerate && i + 1 == a.n_iter) break;
         const uint32_t pos = a.pos0 + i, S = a.s0 + i;
         for (int l = 0; l < layers; ++l) {
-            const int g = int(i) * layers + l;
-            for (int ph = kPhQkv; ph <= kPhMlp; ++ph) {
-                k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, ph, l, g, pos, S);
+            for (int ph = kPhQkv; ph <= kPhMp; ++ph) {
+                k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, ph, l, pos, S);
                 ++*launches;
             }
         }
-        k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, layers, int(i) * layers + layers, pos, S);
+        k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, layers, pos, S);
         ++*launches;
     }
     k_layer_finish<<<1, 1, 0, s>>>(a);
@@ -982,7 +994,7 @@ cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cud
 }
 
 cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s) {
-    k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, 0, 0, 0, 0);
+    k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, 0, 0, 0);
     return cudaGetLastError();
 }
 

@@ -218,13 +218,10 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
                                  "mlp.c_fc.weight", "mlp.c_fc.bias", "mlp.c_proj.weight", "mlp.c_proj.bias"};
     for (uint32_t i = 0; i < layers; ++i)
         for (const char* n : per_layer) idx.push_back(add("gpt.gpt.h." + std::to_string(i) + "." + n));
-    // mlp.c_proj is also kept in its bundle layout [5120, 1280] for the decode
-    // split-K product; the transposed copy serves the prefill GEMM.
-    std::vector<size_t> mpT_off(layers);
-    for (uint32_t i = 0; i < layers; ++i) {
-        mpT_off[i] = total;
-        total += align256(size_t(5120) * 1280 * 4);
-    }
+    // the decode's [gamma, beta] packs: two per layer, two for the head
+    const size_t kRow = size_t(1280) * 4;
+    const size_t pack_off = total;
+    total += (size_t(layers) + 1) * 4 * kRow;
     c->d_weights = dev_alloc<char>(total, "weight allocation");
     c->weight_bytes = total;
 
@@ -237,11 +234,6 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
             const bool is_conv = t.name.rfind("gpt.gpt.h.", 0) == 0 && t.shape.size() == 2;
             if (is_conv) {
                 ck(cudaMemcpy(stage, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
-                const std::string suffix = ".mlp.c_proj.weight";
-                if (t.name.size() > suffix.size() && t.name.compare(t.name.size() - suffix.size(), suffix.size(), suffix) == 0) {
-                    const uint32_t li = uint32_t(std::stoul(t.name.substr(10, t.name.find('.', 10) - 10)));
-                    ck(cudaMemcpy(c->d_weights + mpT_off[li], stage, t.nbytes, cudaMemcpyDeviceToDevice), "weight copy");
-                }
                 ck(itts::launch_transpose(stage, reinterpret_cast<float*>(dst), int(t.shape[0]), int(t.shape[1]),
                                           nullptr),
                    "transpose launch");
@@ -285,8 +277,21 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
         L.b_fc = ptr(o + 9);
         L.w_mp = ptr(o + 10);
         L.b_mp = ptr(o + 11);
-        L.w_mpT = reinterpret_cast<const float*>(c->d_weights + mpT_off[i]);
     }
+    // fill the [gamma, beta] packs (device-to-device copies of the uploaded vectors)
+    char* packs = c->d_weights + pack_off;
+    auto put = [&](char* dst, const float* g, const float* b) {
+        ck(cudaMemcpy(dst, g, kRow, cudaMemcpyDeviceToDevice), "pack copy");
+        ck(cudaMemcpy(dst + kRow, b, kRow, cudaMemcpyDeviceToDevice), "pack copy");
+        return reinterpret_cast<const float*>(dst);
+    };
+    for (uint32_t i = 0; i < layers; ++i) {
+        itts::LayerW& L = c->hw.layer[i];
+        L.ln1_pack = put(packs + size_t(i) * 4 * kRow, L.ln1_g, L.ln1_b);
+        L.ln2_pack = put(packs + (size_t(i) * 4 + 2) * kRow, L.ln2_g, L.ln2_b);
+    }
+    c->hw.head_pack1 = put(packs + size_t(layers) * 4 * kRow, c->hw.lnf_g, c->hw.lnf_b);
+    c->hw.head_pack2 = put(packs + (size_t(layers) * 4 + 2) * kRow, c->hw.fn_g, c->hw.fn_b);
     const uint64_t per_layer_floats = 19660800ull + 11520ull + 5120ull;
     c->stream_bytes = 4ull * (per_layer_floats * layers + 10488320ull + 8194ull + 5120ull + 2560ull);
 }
@@ -302,26 +307,27 @@ void alloc_buffers(itts_gpt_ctx* c) {
     c->d_r = c->d_att + T * kW;
     c->d_qkv = c->d_r + T * kW;
     c->d_ff = c->d_qkv + T * 3840;
-    // decode activations (each region 256-byte aligned): qkv, r[2], acc[2]
-    // (8-byte), logits, attention partials, control block
-    const size_t sizes[6] = {3840 * 4, 2 * kW * 4, 2 * kW * 8, 8448 * 4, size_t(kH) * 256 * 66 * 4,
+    // decode activations (each region 256-byte aligned): qkv, h, hm, f, logits,
+    // attention partials, control block
+    const size_t sizes[7] = {3840 * 4, kW * 4, kW * 4, 5120 * 4, 8448 * 4, size_t(kH) * 256 * 68 * 4,
                              sizeof(itts::DecodeCtl)};
     size_t total = 0;
     for (size_t s : sizes) total += align256(s);
     c->d_act = reinterpret_cast<float*>(dev_alloc<char>(total, "decode buffers"));
     char* p = reinterpret_cast<char*>(c->d_act);
-    char* regions[6];
-    for (int i = 0; i < 6; ++i) {
+    char* regions[7];
+    for (int i = 0; i < 7; ++i) {
         regions[i] = p;
         p += align256(sizes[i]);
     }
     c->db.kv = c->d_kv;
     c->db.qkv = reinterpret_cast<float*>(regions[0]);
-    c->db.r = reinterpret_cast<float*>(regions[1]);
-    c->db.acc = reinterpret_cast<long long*>(regions[2]);
-    c->db.logits = reinterpret_cast<float*>(regions[3]);
-    c->db.part = reinterpret_cast<float*>(regions[4]);
-    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[5]);
+    c->db.h = reinterpret_cast<float*>(regions[1]);
+    c->db.hm = reinterpret_cast<float*>(regions[2]);
+    c->db.f = reinterpret_cast<float*>(regions[3]);
+    c->db.logits = reinterpret_cast<float*>(regions[4]);
+    c->db.part = reinterpret_cast<float*>(regions[5]);
+    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[6]);
     c->db.sampler_big = reinterpret_cast<itts::SamplerBig*>(
         dev_alloc<char>(size_t(c->sm_count) * itts::sampler_big_bytes(), "sampler workspace"));
     c->d_sampler_big = c->db.sampler_big;
@@ -382,8 +388,6 @@ itts::DecodeArgs decode_args(itts_gpt_ctx* c) {
 
 void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     reset_ctl(c);
-    // the first layer of a launch accumulates its mlp.c_proj sums into slot 0
-    ck(cudaMemsetAsync(c->db.acc, 0, 2 * kW * sizeof(long long), c->stream), "accumulator reset");
     if (c->mode == 0) {
         ck(itts::launch_decode_persistent(a, c->sm_count, c->stream), "persistent decode launch");
         ++c->launches;
@@ -712,6 +716,8 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
         ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
         if (prop.major < 10) fail(ITTS_ERR_RUNTIME, "this library is built for sm_100a (B200) devices only");
         c->sm_count = prop.multiProcessorCount;
+        // the decode kernel gives each SM at most 64 rows of any matrix (mel_head: 8194)
+        if ((8194 + c->sm_count - 1) / c->sm_count > 64) fail(ITTS_ERR_RUNTIME, "device has too few SMs");
         if (!prop.cooperativeLaunch) fail(ITTS_ERR_RUNTIME, "device lacks cooperative launch");
         int per_sm = 0;
         ck(itts::decode_configure(&per_sm), "decode kernel configuration");

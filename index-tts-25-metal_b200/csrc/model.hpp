@@ -29,8 +29,9 @@ struct LayerW {
     const float *w_o, *b_o;      // [1280, 1280]
     const float *ln2_g, *ln2_b;
     const float *w_fc, *b_fc;    // [5120, 1280]
-    const float *w_mp, *b_mp;    // [1280, 5120] (prefill GEMM)
-    const float *w_mpT;          // [5120, 1280]: the bundle's Conv1D layout (decode split-K)
+    const float *w_mp, *b_mp;    // [1280, 5120]
+    // Contiguous [gamma, beta] copies of ln_1 and ln_2, one bulk copy each.
+    const float *ln1_pack, *ln2_pack;
 };
 
 struct ModelW {
@@ -40,6 +41,8 @@ struct ModelW {
     const float *fn_g, *fn_b;    // gpt.final_norm
     const float *w_head, *b_head;  // gpt.mel_head [8194, 1280] (nn.Linear layout)
     const float *mel_emb, *mel_pos;
+    // [ln_f gamma, beta], [final_norm gamma, beta]
+    const float *head_pack1, *head_pack2;
 };
 
 // Sampling options after GenerationOptions validation (gpt_sampling.cpp:168-173).
@@ -71,10 +74,11 @@ struct SamplerBig;
 struct DecodeBuffers {
     float* kv;        // [layer][K|V][head][4096][64] fp32
     float* qkv;       // [3840]
-    float* r;         // [2][1280] residual after attention, by layer parity
-    long long* acc;   // [2][1280] mlp.c_proj sums, 2^-32 fixed point, by layer parity
+    float* h;         // [1280] residual stream leaving the last finished layer
+    float* hm;        // [1280] residual stream after the attention block
+    float* f;         // [5120] GELU(c_fc) of the current layer
     float* logits;    // [8194]
-    float* part;      // split-K attention partials [20 * 256 * 66]
+    float* part;      // split-K attention partials [20 * 256 * 68]
     SamplerBig* sampler_big;  // one large-survivor workspace per CTA
     DecodeCtl* ctl;
 };
