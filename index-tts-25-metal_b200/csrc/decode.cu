@@ -42,9 +42,20 @@ namespace itts {
 
 // ------------------------------------------------------------ weight ring
 constexpr int kRowBytes = kWidth * 4;              // every streamed row has 1280 fp32
-constexpr int kRowsPerSlot = 4;
-constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 20 KB
-constexpr int kSlots = 10;
+constexpr int kRowsPerSlot = 8;                        // rows of 1280 per slot
+constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 40 KB
+constexpr int kSlots = 5;
+// Consumer geometry: warp w works on row w / kWarpsPerRow of a slot and on
+// column block w % kWarpsPerRow (kColsPerWarp wide); lane l holds the float2
+// at columns block + 2l + 64j, j < kVec.  A 5120-wide row spans
+// kWarpsPerLong warps with the same per-warp width.
+constexpr int kWarpsPerRow = kWarps / kRowsPerSlot;
+constexpr int kColsPerWarp = kWidth / kWarpsPerRow;
+constexpr int kVec = kColsPerWarp / 64;
+constexpr int kLongPerSlot = kSlotBytes / (kFfn * 4);
+constexpr int kWarpsPerLong = kWarps / kLongPerSlot;
+static_assert(kWarpsPerRow * kRowsPerSlot == kWarps && kColsPerWarp % 64 == 0, "slot geometry");
+static_assert(kWarpsPerLong * kColsPerWarp == kFfn, "5120-wide rows use the same per-warp width");
 
 struct Ring {
     __align__(128) unsigned char data[kSlots][kSlotBytes];
@@ -79,12 +90,13 @@ constexpr int kMaxChunks = 8;       // key chunks per head (partials merged per 
 
 struct PhaseSmem {
     float red[32];
+    float wstat[kWarps][2];  // LayerNorm: per-warp (mean, M2)
     union {
-        float rowred[kMaxRowsPerCta][4];  // 1280-wide rows: sums of the four column quarters
-        float longred[16][kWarps];        // 5120-wide rows: sums of the sixteen warps' columns
+        float rowred[kMaxRowsPerCta][kWarpsPerRow];  // 1280-wide rows: block sums
+        float longred[16][kWarpsPerLong];            // 5120-wide rows: block sums
     };
     float f[kMaxRowsPerCta];          // this CTA's GELU outputs
-    __align__(16) float xin[kWidth];  // residual stream entering the layer (pre-LN1)
+    __align__(16) float xin[kWidth];  // staged input vector (phase A: the layer input, kept for phase C)
     union {                           // phase B's warp states / phase C's merged heads
         float wo[kWarps][kHeadDim];
         __align__(16) float attn[kWidth];
@@ -128,11 +140,21 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
         : "memory");
     return done != 0;
 }
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
+// L2 policy of the streamed weights: evicted first, so that one step's 1.9 GB
+// sweep does not push the KV cache, the activations and the kernel's own
+// instructions out of L2.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
 }
 
 // Bounded wait for a ring slot; every thread waits.  The spin touches no
@@ -195,6 +217,7 @@ struct PfCursor {
     uint32_t off, seg_bytes;
     unsigned long long pos;  // schedule bytes passed so far
     const char* p;
+    uint64_t policy;
 };
 
 constexpr uint32_t kPfChunk = 32768;
@@ -213,7 +236,10 @@ __device__ __forceinline__ bool pf_advance(const ModelW& w, const Rows& rows, in
         seg_of(w, rows, c.k, c.p, c.seg_bytes);
     }
     const uint32_t n = min(c.seg_bytes - c.off, kPfChunk);
-    if (issue) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c.p + c.off), "r"(n) : "memory");
+    if (issue)
+        asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(c.p + c.off), "r"(n),
+                     "l"(c.policy)
+                     : "memory");
     c.off += n;
     c.pos += n;
     return true;
@@ -253,7 +279,8 @@ __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Ro
     uint32_t j = 0, parity = 0;
     int s = 0;
     unsigned long long issued = 0;  // schedule bytes issued into the ring
-    PfCursor pf{0, k0 - 1, 0, 0, 0, nullptr};
+    const uint64_t policy = evict_first_policy();
+    PfCursor pf{0, k0 - 1, 0, 0, 0, nullptr, policy};
     for (int step = 0; step < n_steps; ++step) {
         for (int k = k0; k < k1; ++k) {
             const char* p;
@@ -265,7 +292,7 @@ __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Ro
                     !wait_empty(R, s, parity ^ 1u, status, j, w, rows, k0, k1, n_steps, pf, issued))
                     goto done;
                 mbar_expect_tx(&R.full[s], n);
-                bulk_g2s(R.data[s], p + off, n, &R.full[s]);
+                bulk_g2s(R.data[s], p + off, n, &R.full[s], policy);
                 issued += n;
                 ++j;
                 R.issued = j;
@@ -337,35 +364,74 @@ __device__ __forceinline__ void slot_release(Ctx& cx) {
     ++cx.k;
 }
 
-// Input-vector layout of the GEMVs: thread t owns columns 2*(t%128) + 256*j
-// (+1), j < 5, so each 128-thread group holds the whole 1280-vector once and a
-// 4-row slot keeps 4 groups busy.
-__device__ __forceinline__ int col_of(int j) { return 2 * (threadIdx.x & 127) + 256 * j; }
+// Input-vector layout of the 1280-wide GEMVs: the kWarpsPerRow warps of a
+// row hold the whole vector once (kVec float2 per lane).
+__device__ __forceinline__ int col_of(int j) {
+    return kColsPerWarp * ((threadIdx.x >> 5) % kWarpsPerRow) + 2 * (threadIdx.x & 31) + 64 * j;
+}
 
-// LayerNorm of the vector in `x` (statistics over group 0), gamma/beta at
-// g/b (shared memory).  Two-pass mean and centred variance, eps inside the
-// root (kernels.metal:618-669).
-__device__ void layernorm2(float2 (&x)[5], const float* g, const float* b, float* red) {
-    const bool owner = threadIdx.x < 128;
-    float s = 0.f;
-    if (owner) {
+// Chan et al.'s pairwise update of (mean, M2) for two halves of equal size n.
+__device__ __forceinline__ void chan_merge(float& m, float& M2, float mb, float M2b, float n) {
+    const float d = mb - m;
+    m = m + 0.5f * d;
+    M2 = (M2 + M2b) + d * d * (0.5f * n);
+}
+
+// LayerNorm of the vector in `x`, gamma/beta at g/b (shared memory), eps
+// inside the root (kernels.metal:618-669).  Every group of kWarpsPerRow warps
+// holds the whole vector, so each group computes the statistics on its own:
+// per-thread mean and centred sum of squares, merged pairwise across lanes
+// and then across the group's warps (one group barrier), the same operations
+// in the same order in every group.
+__device__ void layernorm2(float2 (&x)[kVec], const float* g, const float* b, float (*wstat)[2]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m = 0.f;
 #pragma unroll
-        for (int j = 0; j < 5; ++j) s += x[j].x + x[j].y;
+    for (int j = 0; j < kVec; ++j) m += x[j].x + x[j].y;
+    m *= 1.0f / (2 * kVec);
+    float M2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        const float a = x[j].x - m, c = x[j].y - m;
+        M2 = fmaf(a, a, M2);
+        M2 = fmaf(c, c, M2);
     }
-    const float mean = cblock_sum(s, red) * (1.0f / kWidth);
-    float v = 0.f;
-    if (owner) {
+    float n = 2 * kVec;
 #pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            const float a = x[j].x - mean, c = x[j].y - mean;
-            v = fmaf(a, a, v);
-            v = fmaf(c, c, v);
+    for (int o = 1; o < 32; o <<= 1) {  // lanes: (l, l^o) with the lower lane first
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o), M2o = __shfl_xor_sync(0xffffffffu, M2, o);
+        if (lane & o) {
+            float mm = mo, MM = M2o;
+            chan_merge(mm, MM, m, M2, n);
+            m = mm;
+            M2 = MM;
+        } else {
+            chan_merge(m, M2, mo, M2o, n);
         }
+        n *= 2.f;
     }
-    const float var = cblock_sum(v, red) * (1.0f / kWidth);
+    if (lane == 0) {
+        wstat[warp][0] = m;
+        wstat[warp][1] = M2;
+    }
+    const int grp = warp / kWarpsPerRow, w0 = grp * kWarpsPerRow;
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "n"(32 * kWarpsPerRow) : "memory");
+    float gm[kWarpsPerRow], gM[kWarpsPerRow];
+#pragma unroll
+    for (int i = 0; i < kWarpsPerRow; ++i) {
+        gm[i] = wstat[w0 + i][0];
+        gM[i] = wstat[w0 + i][1];
+    }
+#pragma unroll
+    for (int k = 1; k < kWarpsPerRow; k <<= 1) {  // warps of the group, pairwise tree
+#pragma unroll
+        for (int q = 0; q < kWarpsPerRow; q += 2 * k) chan_merge(gm[q], gM[q], gm[q + k], gM[q + k], n);
+        n *= 2.f;
+    }
+    const float mean = gm[0], var = gM[0] * (1.0f / kWidth);
     const float inv = 1.0f / sqrtf(var + kLnEps);
 #pragma unroll
-    for (int j = 0; j < 5; ++j) {
+    for (int j = 0; j < kVec; ++j) {
         const int c = col_of(j);
         x[j].x = (x[j].x - mean) * inv * g[c] + b[c];
         x[j].y = (x[j].y - mean) * inv * g[c + 1] + b[c + 1];
@@ -380,23 +446,24 @@ __device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool& abort, int w
     return slot;
 }
 
-// y[row] = W[row, :] . x for `nrows` streamed rows (4 per slot).  Warp w takes
-// row w/4 of each slot and column quarter w%4; the quarter sums stay in shared
-// memory and are added once, after the last slot, when epi(row, y) runs on
-// consumer thread `row`.  No CTA-wide barrier inside the loop.
+// y[row] = W[row, :] . x for `nrows` streamed 1280-wide rows (kRowsPerSlot
+// per slot).  The kWarpsPerRow block sums of a row stay in shared memory and
+// are added once, after the last slot, when epi(row, y) runs on consumer
+// thread `row`.  No CTA-wide barrier inside the loop.
 template <class Epi>
-__device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[5], int where, Epi epi) {
-    const int t = threadIdx.x, rr = t >> 7, q = (t >> 5) & 3, tig = t & 127, lane = t & 31;
+__device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int rr = warp / kWarpsPerRow, q = warp % kWarpsPerRow;
     bool ok = true;
     for (int r0 = 0; r0 < nrows && ok; r0 += kRowsPerSlot) {
         const float* slot = slot_wait(cx, ok, where);
         if (!ok) break;
         if (r0 + rr < nrows) {
-            const float2* w = reinterpret_cast<const float2*>(slot + rr * kWidth) + tig;
+            const float2* w = reinterpret_cast<const float2*>(slot + rr * kWidth + q * kColsPerWarp) + lane;
             float acc = 0.f;
 #pragma unroll
-            for (int j = 0; j < 5; ++j) {
-                const float2 wv = w[j * 128];
+            for (int j = 0; j < kVec; ++j) {
+                const float2 wv = w[j * 32];
                 acc = fmaf(wv.x, x[j].x, acc);
                 acc = fmaf(wv.y, x[j].y, acc);
             }
@@ -408,60 +475,88 @@ __device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[5], int where, 
     if (csync_or(!ok)) return false;
     if (t < nrows) {
         const float* s = cx.sm.rowred[t];
-        epi(t, (s[0] + s[1]) + (s[2] + s[3]));
+        float v = s[0];
+#pragma unroll
+        for (int i = 1; i < kWarpsPerRow; ++i) v += s[i];
+        epi(t, v);
     }
     return true;
 }
 
-// The residual stream entering in-step layer `li` (li = layers: the input of
-// the head), in x's layout: li = 0 the token embedding (gpt_build_current,
-// kernels.metal:1310-1325), otherwise the previous layer's output h.
-__device__ __forceinline__ void load_resid(const DecodeArgs& a, const ModelW& w, int li, uint32_t token, uint32_t pos,
-                                           float2 (&x)[5]) {
-#pragma unroll
-    for (int j = 0; j < 5; ++j) {
-        const int c = col_of(j);
-        if (a.head_src && li == w.layers) {  // prefill: the last hidden row
-            x[j] = __ldcg(reinterpret_cast<const float2*>(a.head_src + c));
-        } else if (li == 0) {
-            const float2 e = __ldg(reinterpret_cast<const float2*>(w.mel_emb + (size_t)token * kWidth + c));
-            const float2 p = __ldg(reinterpret_cast<const float2*>(w.mel_pos + (size_t)pos * kWidth + c));
-            x[j] = make_float2(e.x + p.x, e.y + p.y);
-        } else {
-            x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.h + c));
-        }
+// Stages a 1280-vector in shared memory (threads < 320 copy a float4 each;
+// the caller's next consumer barrier publishes it): the residual stream
+// entering in-step layer `li` (li = layers: the input of the head), that is
+// li = 0 the token embedding (gpt_build_current, kernels.metal:1310-1325),
+// otherwise the previous layer's output h.
+__device__ __forceinline__ void stage_resid(const DecodeArgs& a, const ModelW& w, int li, uint32_t token,
+                                            uint32_t pos, float* dst) {
+    const int t = threadIdx.x;
+    if (t >= kWidth / 4) return;
+    float4 v;
+    if (a.head_src && li == w.layers) {  // prefill: the last hidden row
+        v = __ldcg(reinterpret_cast<const float4*>(a.head_src) + t);
+    } else if (li == 0) {
+        const float4 e = __ldg(reinterpret_cast<const float4*>(w.mel_emb + (size_t)token * kWidth) + t);
+        const float4 p = __ldg(reinterpret_cast<const float4*>(w.mel_pos + (size_t)pos * kWidth) + t);
+        v = make_float4(e.x + p.x, e.y + p.y, e.z + p.z, e.w + p.w);
+    } else {
+        v = __ldcg(reinterpret_cast<const float4*>(a.b.h) + t);
     }
+    reinterpret_cast<float4*>(dst)[t] = v;
 }
 
-// y[row] = W[row, :] . f for `nrows` streamed 5120-wide rows (one per slot);
-// thread t owns columns 2t + 1024j (+1), j < 5, of f.  The sixteen warp sums of
-// a row are added once, after the last slot, when epi(row, y) runs on thread `row`.
+__device__ __forceinline__ void stage_vec(const float* src, float* dst) {
+    if (threadIdx.x < kWidth / 4)
+        reinterpret_cast<float4*>(dst)[threadIdx.x] = __ldcg(reinterpret_cast<const float4*>(src) + threadIdx.x);
+}
+
+// x in the GEMV layout from a staged vector.
+__device__ __forceinline__ void gather_x(const float* v, float2 (&x)[kVec]) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) x[j] = *reinterpret_cast<const float2*>(v + col_of(j));
+}
+
+// Input-vector layout of the 5120-wide GEMV (mlp.c_proj over f).
+__device__ __forceinline__ int long_col_of(int j) {
+    return kColsPerWarp * ((threadIdx.x >> 5) % kWarpsPerLong) + 2 * (threadIdx.x & 31) + 64 * j;
+}
+
+// y[row] = W[row, :] . f for `nrows` streamed 5120-wide rows (kLongPerSlot
+// per slot); the kWarpsPerLong block sums of a row are added once, after the
+// last slot, when epi(row, y) runs on thread `row`.
 template <class Epi>
-__device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[5], int where, Epi epi) {
+__device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int rr = warp / kWarpsPerLong, q = warp % kWarpsPerLong;
     bool ok = true;
-    for (int r = 0; r < nrows && ok; ++r) {
+    for (int r0 = 0; r0 < nrows && ok; r0 += kLongPerSlot) {
         const float* slot = slot_wait(cx, ok, where);
         if (!ok) break;
-        const float2* w = reinterpret_cast<const float2*>(slot) + t;
-        float acc = 0.f;
+        if (r0 + rr < nrows) {
+            const float2* w = reinterpret_cast<const float2*>(slot + rr * kFfn + q * kColsPerWarp) + lane;
+            float acc = 0.f;
 #pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            const float2 wv = w[j * kThreads];
-            acc = fmaf(wv.x, x[j].x, acc);
-            acc = fmaf(wv.y, x[j].y, acc);
+            for (int j = 0; j < kVec; ++j) {
+                const float2 wv = w[j * 32];
+                acc = fmaf(wv.x, x[j].x, acc);
+                acc = fmaf(wv.y, x[j].y, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) cx.sm.longred[r0 + rr][q] = acc;
         }
-        acc = warp_sum(acc);
-        if (lane == 0) cx.sm.longred[r][warp] = acc;
         slot_release(cx);
     }
     if (csync_or(!ok)) return false;
     if (t < nrows) {
         const float* s = cx.sm.longred[t];
-        float v[8];
+        float v[kWarpsPerLong / 2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = s[2 * i] + s[2 * i + 1];
-        epi(t, ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7])));
+        for (int i = 0; i < kWarpsPerLong / 2; ++i) v[i] = s[2 * i] + s[2 * i + 1];
+#pragma unroll
+        for (int w = kWarpsPerLong / 4; w >= 1; w >>= 1)
+#pragma unroll
+            for (int i = 0; i < w; ++i) v[i] = v[2 * i] + v[2 * i + 1];
+        epi(t, v[0]);
     }
     return true;
 }
@@ -471,15 +566,13 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.q0, nrows = cx.rows.q1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.layer[li].b_qkv + r0 + t) : 0.f;  // used after the last slot
-    float2 x[5];
-    load_resid(a, cx.w, li, token, pos, x);
+    stage_resid(a, cx.w, li, token, pos, cx.sm.xin);  // kept for phase C's residual
     bool abort;
     const float* slot = ln_slot_wait(cx, abort, 10 + li);
     if (abort) return false;
-    if (t < 128)
-#pragma unroll
-        for (int j = 0; j < 5; ++j) *reinterpret_cast<float2*>(&cx.sm.xin[col_of(j)]) = x[j];
-    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    float2 x[kVec];
+    gather_x(cx.sm.xin, x);
+    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.qkv + r0;
     return gemv_slots(cx, nrows, x, 40 + li, [&](int row, float v) { out[row] = v + bias; });
@@ -604,42 +697,46 @@ __device__ bool phase_oproj(Ctx& cx, int li, uint32_t token, uint32_t pos, uint3
         else
             res = __ldcg(a.b.h + r);
     }
-    // merge the split-K attention partials: warp w merges heads w and w + 16,
-    // lane l outputs 2l, 2l+1; all loads of a head's partials are in flight together
+    // merge the split-K attention partials: thread t < 320 produces outputs
+    // 4t..4t+3 (head 4t/64); all loads of its partials are in flight together
     const uint32_t keys = S + 1;
     const uint32_t ch = attn_chunk(keys, cx.ncta);
     const int nch = int((keys + ch - 1) / ch);
-    const int lane = t & 31;
-    for (int h = t >> 5; h < kHeads; h += kWarps) {
+    if (t < kWidth / 4) {
+        const int h = (4 * t) / kHeadDim, d = (4 * t) % kHeadDim;
         const float* ph = a.b.part + (size_t)h * nch * kPartStride;
-        float2 ml[kMaxChunks], ov[kMaxChunks];
+        float2 ml[kMaxChunks];
+        float4 ov[kMaxChunks];
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c) {
             if (c < nch) {
                 ml[c] = __ldcg(reinterpret_cast<const float2*>(ph + c * kPartStride));
-                ov[c] = __ldcg(reinterpret_cast<const float2*>(ph + c * kPartStride + 4) + lane);
+                ov[c] = __ldcg(reinterpret_cast<const float4*>(ph + c * kPartStride + 4 + d));
             }
         }
         float M = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c)
             if (c < nch) M = fmaxf(M, ml[c].x);
-        float Ls = 0.f, o0 = 0.f, o1 = 0.f;
+        float Ls = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c) {
             if (c < nch) {
                 const float e = expf(ml[c].x - M);
                 Ls = fmaf(e, ml[c].y, Ls);
-                o0 = fmaf(e, ov[c].x, o0);
-                o1 = fmaf(e, ov[c].y, o1);
+                o.x = fmaf(e, ov[c].x, o.x);
+                o.y = fmaf(e, ov[c].y, o.y);
+                o.z = fmaf(e, ov[c].z, o.z);
+                o.w = fmaf(e, ov[c].w, o.w);
             }
         }
-        *reinterpret_cast<float2*>(&cx.sm.attn[h * kHeadDim + 2 * lane]) = make_float2(o0 / Ls, o1 / Ls);
+        *reinterpret_cast<float4*>(&cx.sm.attn[4 * t]) = make_float4(o.x / Ls, o.y / Ls, o.z / Ls, o.w / Ls);
     }
     csync();
-    float2 x[5];
+    float2 x[kVec];
 #pragma unroll
-    for (int j = 0; j < 5; ++j) x[j] = *reinterpret_cast<const float2*>(&cx.sm.attn[col_of(j)]);
+    for (int j = 0; j < kVec; ++j) x[j] = *reinterpret_cast<const float2*>(&cx.sm.attn[col_of(j)]);
     float* out = a.b.hm + r0;
     return gemv_slots(cx, nrows, x, 70 + li, [&](int row, float v) { out[row] = res + (v + bias); });
 }
@@ -649,13 +746,13 @@ __device__ bool phase_fc(Ctx& cx, int li) {
     const DecodeArgs& a = cx.a;
     const int f0 = cx.rows.f0, nf = cx.rows.f1 - f0, t = threadIdx.x;
     const float bias = t < nf ? __ldg(cx.w.layer[li].b_fc + f0 + t) : 0.f;
-    float2 x[5];
-#pragma unroll
-    for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.hm + col_of(j)));
+    stage_vec(a.b.hm, cx.sm.xin);
     bool abort;
     const float* slot = ln_slot_wait(cx, abort, 100 + li);
     if (abort) return false;
-    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    float2 x[kVec];
+    gather_x(cx.sm.xin, x);
+    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.f + f0;
     return gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); });
@@ -670,9 +767,9 @@ __device__ bool phase_mp(Ctx& cx, int li) {
         bias = __ldg(cx.w.layer[li].b_mp + r0 + t);
         res = __ldcg(a.b.hm + r0 + t);
     }
-    float2 x[5];
+    float2 x[kVec];
 #pragma unroll
-    for (int j = 0; j < 5; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.f) + t + j * kThreads);
+    for (int j = 0; j < kVec; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.f + long_col_of(j)));
     float* out = a.b.h + r0;
     return gemv_long_slots(cx, nrows, x, 160 + li, [&](int row, float v) { out[row] = res + (v + bias); });
 }
@@ -682,46 +779,53 @@ __device__ bool phase_head(Ctx& cx, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.h0, nrows = cx.rows.h1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.b_head + r0 + t) : 0.f;
-    float2 x[5];
-    load_resid(a, cx.w, cx.w.layers, token, pos, x);
+    stage_resid(a, cx.w, cx.w.layers, token, pos, cx.sm.xin);
     bool abort;
     const float* slot = ln_slot_wait(cx, abort, 200);
     if (abort) return false;
-    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    float2 x[kVec];
+    gather_x(cx.sm.xin, x);
+    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     slot = ln_slot_wait(cx, abort, 200);
     if (abort) return false;
-    layernorm2(x, slot, slot + kWidth, cx.sm.red);
+    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.logits + r0;
     return gemv_slots(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
 }
 
 // Grid barrier of the persistent kernel (all CTAs co-resident by the
-// cooperative launch): monotonic arrival counter, bounded spin; true when the
-// kernel must abort (error status or timeout).
+// cooperative launch): thread 0 adds its CTA's arrival with a release
+// reduction and polls the monotonic counter with acquire loads.  The status
+// word is read only when the wait is slow, so an error raised elsewhere ends
+// the wait after kStatusPollNs; true when the kernel must abort.
 __device__ bool grid_barrier(Ctx& cx, unsigned& target, int where) {
     target += gridDim.x;
     csync();
     if (threadIdx.x == 0) {
         unsigned* bar = &cx.a.b.ctl->bar;
         int* status = cx.a.b.ctl->status;
-        __threadfence();
-        atomicAdd(bar, 1u);
-        const unsigned long long t0 = globaltimer_ns();
-        unsigned spins = 0;
-        while (ld_acquire_gpu(bar) < target) {
-            if ((++spins & 31u) == 0) {
-                const unsigned long long dt = globaltimer_ns() - t0;
-                if (dt > kStatusPollNs && ld_volatile(status) != 0) break;
-                if (dt > kWaitLimitNs) {
-                    set_status(status, kStatusBarrierTimeout, where, (int)target);
-                    break;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        int abort = 0;
+        if (ld_acquire_gpu(bar) < target) {
+            const unsigned long long t0 = globaltimer_ns();
+            for (unsigned spins = 1; ld_acquire_gpu(bar) < target; ++spins) {
+                if ((spins & 31u) == 0) {
+                    const unsigned long long dt = globaltimer_ns() - t0;
+                    if (dt > kStatusPollNs && ld_volatile(status) != 0) {
+                        abort = 1;
+                        break;
+                    }
+                    if (dt > kWaitLimitNs) {
+                        set_status(status, kStatusBarrierTimeout, where, (int)target);
+                        abort = 1;
+                        break;
+                    }
                 }
             }
         }
-        __threadfence();
-        cx.sm.abort = ld_volatile(status) != 0;
+        cx.sm.abort = abort;
     }
     csync();
     return cx.sm.abort != 0;

@@ -14,12 +14,14 @@
 // (fixed thread mapping and reduction order), which lets the persistent
 // decode kernel sample redundantly in all CTAs instead of adding a barrier.
 //
-// Layout: thread t owns the contiguous logits [17 t, 17 t + 17) (482 threads
-// cover the 8194 codes), so index-ordered compaction is one block scan.
-// The k-th largest score is found by a 4-pass 8-bit radix select on order-
-// preserving integer keys; the top-p survivors are sorted with a bitonic sort
-// of 64-bit (score key, index) words; the double-precision sums that fix the
-// reference's rounding order run sequentially in thread 0.
+// Layout: thread t owns the contiguous logits [16 t, 16 t + 16) (four float4
+// loads), thread 511 also the start and stop codes 8192 and 8193, so index-
+// ordered compaction is one block scan.  The k-th largest score is found by a
+// 4-pass 8-bit radix select on order-preserving integer keys with warp-
+// aggregated histogram updates; the top-p survivors are sorted with a bitonic
+// sort of 64-bit (score key, index) words (within one warp for up to 32); the
+// double-precision sums that fix the reference's rounding order run
+// sequentially in thread 0 over values computed in parallel.
 #pragma once
 
 #include "common.cuh"
@@ -27,7 +29,10 @@
 
 namespace itts {
 
-constexpr int kPer = 17;
+constexpr int kPer = 18;  // registers per thread (16, or 18 for the last thread)
+static_assert(16 * kThreads + 2 == kVocab, "sampler layout: 16 codes per thread + 2 in the last");
+__device__ __forceinline__ int elem_base() { return 16 * threadIdx.x; }
+__device__ __forceinline__ int elem_cnt() { return threadIdx.x == kThreads - 1 ? kVocab - 16 * (kThreads - 1) : 16; }
 constexpr int kBits = (kVocab + 31) / 32;
 constexpr int kSortCap = 16384;  // next power of two >= 8194
 constexpr int kFast = 256;       // survivors handled entirely in shared memory
@@ -43,10 +48,12 @@ struct SamplerSmem {
     uint32_t redu[32];
     uint32_t sel_bin, sel_rem, result;
     int err;
+    double f_total;
     uint32_t f_idx[kFast];
     float f_s[kFast];
     unsigned long long f_key[kFast];
     double f_pr[kFast];
+    double f_q[kFast];  // top-p: exp / total in ascending order
 };
 
 // Workspace for more than kFast survivors (top-p without top-k, or wide ties):
@@ -153,11 +160,16 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
         for (int i = threadIdx.x; i < 256; i += kThreads) sm.hist[i] = 0;
         csync();
 #pragma unroll
-        for (int k = 0; k < kPer; ++k)
-            if (k < cnt) {
-                const uint32_t key = ord_key(s[k]);
-                if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1u);
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t key = ord_key(s[k]);
+            const bool part = k < cnt && (key & mask) == prefix;
+            const unsigned act = __ballot_sync(0xffffffffu, part);
+            if (part) {  // one shared-memory atomic per distinct bin of the warp
+                const uint32_t bin = (key >> shift) & 255u;
+                const unsigned peers = __match_any_sync(act, bin);
+                if (lane == __ffs(peers) - 1) atomicAdd(&sm.hist[bin], (uint32_t)__popc(peers));
             }
+        }
         csync();
         if (warp == 0) {
             uint32_t c[8], sum = 0;
@@ -193,6 +205,23 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
         csync();
     }
     return key_float(prefix);
+}
+
+// Ascending sort of key[0..32) by warp 0 in registers; the caller publishes
+// the result with a consumer barrier.
+__device__ inline void warp_sort32_asc(unsigned long long* key) {
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    unsigned long long v = key[lane];
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool keep_min = ((lane & j) == 0) == ((lane & k) == 0);
+            v = keep_min ? (o < v ? o : v) : (o > v ? o : v);
+        }
+    key[lane] = v;
 }
 
 __device__ inline void bitonic_sort_asc(unsigned long long* key, int P) {
@@ -262,11 +291,24 @@ __device__ inline uint32_t block_argmax(const float (&s)[kPer], int base, int cn
 __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o, uint64_t draw, bool greedy,
                                        SamplerSmem& sm, SamplerBig* big, float* out_scores, int* status) {
     const int tid = threadIdx.x;
-    const int base = tid * kPer;
-    const int cnt = max(0, min(kPer, kVocab - base));
+    const int base = elem_base(), cnt = elem_cnt();
     float s[kPer];
+    if ((reinterpret_cast<uintptr_t>(logits) & 15u) == 0) {
+        const float4* p4 = reinterpret_cast<const float4*>(logits + base);
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) s[k] = k < cnt ? __ldcg(logits + base + k) : -INFINITY;
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = __ldcg(p4 + q);
+            s[4 * q] = v.x;
+            s[4 * q + 1] = v.y;
+            s[4 * q + 2] = v.z;
+            s[4 * q + 3] = v.w;
+        }
+#pragma unroll
+        for (int k = 16; k < kPer; ++k) s[k] = k < cnt ? __ldcg(logits + base + k) : -INFINITY;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) s[k] = k < cnt ? __ldcg(logits + base + k) : -INFINITY;
+    }
 
     // repetition penalty (unique history; negative scores are multiplied)
     if (o.rp != 1.0f) {
@@ -336,22 +378,36 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
         int P = 1;
         while (P < (int)n) P <<= 1;
         // (score key, survivor position): position order is index order
-        for (int i = tid; i < P; i += kThreads)
+        const int P_init = P <= 32 ? 32 : P;  // the warp sort reads 32 entries
+        for (int i = tid; i < P_init; i += kThreads)
             key[i] = i < (int)n ? ((unsigned long long)ord_key(sc[i]) << 32) | (uint32_t)i : ~0ull;
         csync();
-        bitonic_sort_asc(key, P);
+        if (P <= 32) {
+            warp_sort32_asc(key);
+            csync();
+        } else {
+            bitonic_sort_asc(key, P);
+        }
         if (tid == 0) {
-            sm.err = 0;
             double total = 0.0;
             for (uint32_t i = 0; i < n; ++i) total += pr ? pr[i] : exp(double(sc[i] - mx));
-            if (!(total > 0.0)) {
-                sm.err = kStatusZeroMass;
-            } else {
+            sm.err = total > 0.0 ? 0 : kStatusZeroMass;
+            sm.f_total = total;
+        }
+        csync();
+        if (pr && !sm.err) {  // each survivor's share, in ascending order (same division as the reference)
+            const double total = sm.f_total;
+            for (uint32_t j = tid; j < n; j += kThreads) sm.f_q[j] = pr[uint32_t(key[j])] / total;
+            csync();
+        }
+        if (tid == 0 && !sm.err) {
+            const double total = sm.f_total;
+            {
                 const double low = 1.0 - double(o.top_p);
                 double cum = 0.0;
                 for (uint32_t j = 0; j < n; ++j) {
                     const uint32_t pos = uint32_t(key[j]);
-                    cum += (pr ? pr[pos] : exp(double(sc[pos] - mx))) / total;
+                    cum += pr ? sm.f_q[j] : exp(double(sc[pos] - mx)) / total;
                     if (cum <= low) {
                         const uint32_t t = idx[pos];
                         sm.removed[t >> 5] |= 1u << (t & 31);
