@@ -102,7 +102,8 @@ struct PhaseSmem {
         __align__(16) float attn[kWidth];
     };
     float wm[kWarps], wl[kWarps];
-    int abort;
+    __align__(16) float qkvh[3 * kHeadDim];  // phase B: q, k, v of the unit's head
+    int abort, last;
 };
 
 struct DecodeSmem {
@@ -438,41 +439,70 @@ __device__ void layernorm2(float2 (&x)[kVec], const float* g, const float* b, fl
     }
 }
 
-// Waits for the slot holding LayerNorm vectors (an abort is taken uniformly).
-__device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool& abort, int where) {
+// Waits for the slot holding LayerNorm vectors; `staged` is this thread's
+// hand-off result, folded in so that an abort is taken uniformly.
+__device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool staged, bool& abort, int where) {
     bool ok;
     const float* slot = slot_wait(cx, ok, where);
-    abort = csync_or(!ok);
+    abort = csync_or(!ok || !staged);
     return slot;
 }
 
-// y[row] = W[row, :] . x for `nrows` streamed 1280-wide rows (kRowsPerSlot
-// per slot).  The kWarpsPerRow block sums of a row stay in shared memory and
-// are added once, after the last slot, when epi(row, y) runs on consumer
-// thread `row`.  No CTA-wide barrier inside the loop.
+constexpr int kMaxSlotsPerPhase = 8;  // 64 rows of 1280 or 16 rows of 5120 per CTA
+
+// Dot products of x with `nrows` streamed rows of kRowLen floats (kRowsPer
+// per slot, kWPR warps per row).  Each warp keeps one partial per slot in a
+// register and the butterflies of all slots run together after the last one,
+// so a slot costs its wait, loads, FMAs and release; block sums go to
+// red[row * kWPR + block].
+template <int kRowLen, int kRowsPer, int kWPR>
+__device__ bool stream_dots(Ctx& cx, int nrows, const float2 (&x)[kVec], float* red, int where) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rr = warp / kWPR, q = warp % kWPR;
+    float acc[kMaxSlotsPerPhase];
+    bool ok = true;
+#pragma unroll
+    for (int si = 0; si < kMaxSlotsPerPhase; ++si) {
+        acc[si] = 0.f;
+        const int r0 = si * kRowsPer;
+        if (r0 < nrows && ok) {
+            const float* slot = slot_wait(cx, ok, where);
+            if (ok) {
+                if (r0 + rr < nrows) {
+                    const float2* w = reinterpret_cast<const float2*>(slot + rr * kRowLen + q * kColsPerWarp) + lane;
+                    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < kVec; ++j) {
+                        const float2 wv = w[j * 32];
+                        a0 = fmaf(wv.x, x[j].x, a0);
+                        a1 = fmaf(wv.y, x[j].y, a1);
+                    }
+                    acc[si] = a0 + a1;
+                }
+                slot_release(cx);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int si = 0; si < kMaxSlotsPerPhase; ++si) acc[si] += __shfl_xor_sync(0xffffffffu, acc[si], o);
+    if (lane == 0)
+#pragma unroll
+        for (int si = 0; si < kMaxSlotsPerPhase; ++si) {
+            const int r = si * kRowsPer + rr;
+            if (r < nrows) red[r * kWPR + q] = acc[si];
+        }
+    return ok;
+}
+
+// y[row] = W[row, :] . x for `nrows` streamed 1280-wide rows; epi(row, y)
+// runs on consumer thread `row` once all slots are consumed.
 template <class Epi>
 __device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int rr = warp / kWarpsPerRow, q = warp % kWarpsPerRow;
-    bool ok = true;
-    for (int r0 = 0; r0 < nrows && ok; r0 += kRowsPerSlot) {
-        const float* slot = slot_wait(cx, ok, where);
-        if (!ok) break;
-        if (r0 + rr < nrows) {
-            const float2* w = reinterpret_cast<const float2*>(slot + rr * kWidth + q * kColsPerWarp) + lane;
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < kVec; ++j) {
-                const float2 wv = w[j * 32];
-                acc = fmaf(wv.x, x[j].x, acc);
-                acc = fmaf(wv.y, x[j].y, acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) cx.sm.rowred[r0 + rr][q] = acc;
-        }
-        slot_release(cx);
-    }
+    const bool ok = stream_dots<kWidth, kRowsPerSlot, kWarpsPerRow>(cx, nrows, x, &cx.sm.rowred[0][0], where);
     if (csync_or(!ok)) return false;
+    const int t = threadIdx.x;
     if (t < nrows) {
         const float* s = cx.sm.rowred[t];
         float v = s[0];
@@ -483,31 +513,83 @@ __device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int wher
     return true;
 }
 
-// Stages a 1280-vector in shared memory (threads < 320 copy a float4 each;
-// the caller's next consumer barrier publishes it): the residual stream
-// entering in-step layer `li` (li = layers: the input of the head), that is
-// li = 0 the token embedding (gpt_build_current, kernels.metal:1310-1325),
-// otherwise the previous layer's output h.
-__device__ __forceinline__ void stage_resid(const DecodeArgs& a, const ModelW& w, int li, uint32_t token,
-                                            uint32_t pos, float* dst) {
+// ------------------------------------------------------ tagged hand-offs
+// A value handed to other CTAs is one 64-bit word (epoch << 32 | float bits)
+// stored with a single-copy-atomic relaxed store; the reader polls the words
+// it needs until all carry the epoch it wants, so the data is its own flag and
+// no grid barrier separates the phases of a layer.  Epoch of in-step layer l
+// of forward step i of a launch: i * layers + l + 1 (0: cleared memory).
+__device__ __forceinline__ void put_tagged(unsigned long long* p, uint32_t epoch, float v) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool has_tag(unsigned long long w, uint32_t epoch) { return uint32_t(w >> 32) == epoch; }
+__device__ __forceinline__ float tagged_value(unsigned long long w) { return __uint_as_float(uint32_t(w)); }
+
+// Polls words p[0..2n) (n 16-byte pairs from p, stride 2) until all carry
+// `epoch`; bounded like every wait (false on timeout or an error status).
+__device__ bool poll_tagged(const unsigned long long* p, int n, uint32_t epoch, float* out, int* status, int where) {
+    ulonglong2 v[2];
+    for (int i = 0; i < n; ++i) v[i] = ld_tagged2(p + 2 * i);
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        bool ready = true;
+        for (int i = 0; i < n; ++i) ready = ready && has_tag(v[i].x, epoch) && has_tag(v[i].y, epoch);
+        if (ready) break;
+        if (it == 0) t0 = globaltimer_ns();
+        if ((it & 15u) == 15u) {
+            const unsigned long long dt = globaltimer_ns() - t0;
+            if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
+            if (dt > kWaitLimitNs) {
+                set_status(status, kStatusBarrierTimeout, where, (int)epoch);
+                return false;
+            }
+        }
+        for (int i = 0; i < n; ++i)
+            if (!(has_tag(v[i].x, epoch) && has_tag(v[i].y, epoch))) v[i] = ld_tagged2(p + 2 * i);
+    }
+    for (int i = 0; i < n; ++i) {
+        out[2 * i] = tagged_value(v[i].x);
+        out[2 * i + 1] = tagged_value(v[i].y);
+    }
+    return true;
+}
+
+// Stages a tagged 1280-vector in shared memory (threads < 320, four words
+// each); the caller's next consumer barrier publishes it.  False on abort.
+__device__ __forceinline__ bool stage_tagged(const unsigned long long* src, uint32_t epoch, float* dst, int* status,
+                                             int where) {
     const int t = threadIdx.x;
-    if (t >= kWidth / 4) return;
-    float4 v;
-    if (a.head_src && li == w.layers) {  // prefill: the last hidden row
-        v = __ldcg(reinterpret_cast<const float4*>(a.head_src) + t);
+    if (t >= kWidth / 4) return true;
+    float v[4];
+    if (!poll_tagged(src + 4 * t, 2, epoch, v, status, where)) return false;
+    *reinterpret_cast<float4*>(dst + 4 * t) = make_float4(v[0], v[1], v[2], v[3]);
+    return true;
+}
+
+// The residual stream entering in-step layer `li` (li = layers: the input of
+// the head), staged in shared memory: li = 0 the token embedding
+// (gpt_build_current, kernels.metal:1310-1325), the prefill's last hidden row
+// for the prefill head, otherwise the previous layer's output h.
+__device__ __forceinline__ bool stage_resid(const DecodeArgs& a, const ModelW& w, int li, uint32_t epoch,
+                                            uint32_t token, uint32_t pos, float* dst, int where) {
+    const int t = threadIdx.x;
+    if (t >= kWidth / 4) return true;
+    if (a.head_src && li == w.layers) {
+        reinterpret_cast<float4*>(dst)[t] = __ldcg(reinterpret_cast<const float4*>(a.head_src) + t);
     } else if (li == 0) {
         const float4 e = __ldg(reinterpret_cast<const float4*>(w.mel_emb + (size_t)token * kWidth) + t);
         const float4 p = __ldg(reinterpret_cast<const float4*>(w.mel_pos + (size_t)pos * kWidth) + t);
-        v = make_float4(e.x + p.x, e.y + p.y, e.z + p.z, e.w + p.w);
+        reinterpret_cast<float4*>(dst)[t] = make_float4(e.x + p.x, e.y + p.y, e.z + p.z, e.w + p.w);
     } else {
-        v = __ldcg(reinterpret_cast<const float4*>(a.b.h) + t);
+        return stage_tagged(a.b.h, epoch - 1, dst, a.b.ctl->status, where);
     }
-    reinterpret_cast<float4*>(dst)[t] = v;
-}
-
-__device__ __forceinline__ void stage_vec(const float* src, float* dst) {
-    if (threadIdx.x < kWidth / 4)
-        reinterpret_cast<float4*>(dst)[threadIdx.x] = __ldcg(reinterpret_cast<const float4*>(src) + threadIdx.x);
+    return true;
 }
 
 // x in the GEMV layout from a staged vector.
@@ -522,31 +604,12 @@ __device__ __forceinline__ int long_col_of(int j) {
 }
 
 // y[row] = W[row, :] . f for `nrows` streamed 5120-wide rows (kLongPerSlot
-// per slot); the kWarpsPerLong block sums of a row are added once, after the
-// last slot, when epi(row, y) runs on thread `row`.
+// per slot); epi(row, y) runs on thread `row` once all slots are consumed.
 template <class Epi>
 __device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int rr = warp / kWarpsPerLong, q = warp % kWarpsPerLong;
-    bool ok = true;
-    for (int r0 = 0; r0 < nrows && ok; r0 += kLongPerSlot) {
-        const float* slot = slot_wait(cx, ok, where);
-        if (!ok) break;
-        if (r0 + rr < nrows) {
-            const float2* w = reinterpret_cast<const float2*>(slot + rr * kFfn + q * kColsPerWarp) + lane;
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < kVec; ++j) {
-                const float2 wv = w[j * 32];
-                acc = fmaf(wv.x, x[j].x, acc);
-                acc = fmaf(wv.y, x[j].y, acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) cx.sm.longred[r0 + rr][q] = acc;
-        }
-        slot_release(cx);
-    }
+    const bool ok = stream_dots<kFfn, kLongPerSlot, kWarpsPerLong>(cx, nrows, x, &cx.sm.longred[0][0], where);
     if (csync_or(!ok)) return false;
+    const int t = threadIdx.x;
     if (t < nrows) {
         const float* s = cx.sm.longred[t];
         float v[kWarpsPerLong / 2];
@@ -562,20 +625,20 @@ __device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int
 }
 
 // ---------------------------------------------------------------- phases
-__device__ bool phase_qkv(Ctx& cx, int li, uint32_t token, uint32_t pos) {
+__device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.q0, nrows = cx.rows.q1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.layer[li].b_qkv + r0 + t) : 0.f;  // used after the last slot
-    stage_resid(a, cx.w, li, token, pos, cx.sm.xin);  // kept for phase C's residual
+    const bool staged = stage_resid(a, cx.w, li, epoch, token, pos, cx.sm.xin, 10 + li);  // kept for phase C
     bool abort;
-    const float* slot = ln_slot_wait(cx, abort, 10 + li);
+    const float* slot = ln_slot_wait(cx, staged, abort, 10 + li);
     if (abort) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
-    float* out = a.b.qkv + r0;
-    return gemv_slots(cx, nrows, x, 40 + li, [&](int row, float v) { out[row] = v + bias; });
+    unsigned long long* out = a.b.qkv + r0;
+    return gemv_slots(cx, nrows, x, 40 + li, [&](int row, float v) { put_tagged(out + row, epoch, v + bias); });
 }
 
 // Key chunk of one attention unit: a multiple of 16 keys, at most kMaxChunks
@@ -587,52 +650,67 @@ __device__ __forceinline__ uint32_t attn_chunk(uint32_t keys, int ncta) {
 }
 
 // Split-K attention for the current query over keys [0, S] (S cached + the
-// current key from qkv).  Unit = (head, chunk of ch keys); warp w takes keys
-// w, w+16, ... of the chunk with an online softmax (K and V fetched together);
-// the 16 warp states are merged in shared memory into one partial
-// (max, sum, 64 outputs) per unit, merged across chunks in phase C.  The unit
-// holding key S appends this token's K/V to the cache.
-__device__ void phase_attn(Ctx& cx, int li, uint32_t S) {
+// current key), kernels.metal:2064-2145.  Unit = (head, chunk of ch keys);
+// warp w takes keys w, w+16, ... of the chunk with an online softmax (K and V
+// fetched together); the 16 warp states are merged into one partial (max,
+// sum, 64 outputs).  The unit holding key S appends this token's K/V to the
+// cache.  A per-head arrival counter (acq_rel) finds the last unit of a head,
+// which merges the head's partials and hands the 64 outputs on as tagged
+// words; the others go straight on to phase C.
+__device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
     const DecodeArgs& a = cx.a;
+    int* status = a.b.ctl->status;
     const uint32_t keys = S + 1;
     const uint32_t ch = attn_chunk(keys, cx.ncta);
     const uint32_t nch = (keys + ch - 1) / ch, units = kHeads * nch;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    float* qkv = cx.sm.qkvh;
     for (uint32_t u = cx.cta; u < units; u += cx.ncta) {
         const uint32_t h = u / nch, c = u % nch, k0 = c * ch, k1 = min(k0 + ch, keys);
         float* Kc = a.b.kv + (((size_t)li * 2 + 0) * kHeads + h) * (size_t)kKvCapacity * kHeadDim;
         float* Vc = a.b.kv + (((size_t)li * 2 + 1) * kHeads + h) * (size_t)kKvCapacity * kHeadDim;
-        const float* kcur = a.b.qkv + kWidth + h * kHeadDim;
-        const float* vcur = a.b.qkv + 2 * kWidth + h * kHeadDim;
-        const float2 q = __ldcg(reinterpret_cast<const float2*>(a.b.qkv + h * kHeadDim) + lane);
+        bool ok = true;
+        if (t < 48) {  // q, k, v of head h: 3 x 16 threads x 4 words
+            const int part = t >> 4, q4 = t & 15;
+            float v[4];
+            ok = poll_tagged(a.b.qkv + part * kWidth + h * kHeadDim + 4 * q4, 2, epoch, v, status, 60 + li);
+            *reinterpret_cast<float4*>(qkv + part * kHeadDim + 4 * q4) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        if (csync_or(!ok)) return false;
+        const float* kcur = qkv + kHeadDim;
+        const float* vcur = qkv + 2 * kHeadDim;
+        const float2 q = *reinterpret_cast<const float2*>(qkv + 2 * lane);
         float m = -INFINITY, l = 0.f;
         float2 o = make_float2(0.f, 0.f);
         for (uint32_t kb = k0 + warp; kb < k1; kb += 4 * kWarps) {
             float2 kv[4], vv[4];
-            float s[4];
+            float s4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t kk = kb + i * kWarps;
                 if (kk < k1) {
-                    const float* kr = kk < S ? Kc + (size_t)kk * kHeadDim : kcur;
-                    const float* vr = kk < S ? Vc + (size_t)kk * kHeadDim : vcur;
-                    kv[i] = __ldcg(reinterpret_cast<const float2*>(kr) + lane);
-                    vv[i] = __ldcg(reinterpret_cast<const float2*>(vr) + lane);
+                    if (kk < S) {
+                        kv[i] = __ldcg(reinterpret_cast<const float2*>(Kc + (size_t)kk * kHeadDim) + lane);
+                        vv[i] = __ldcg(reinterpret_cast<const float2*>(Vc + (size_t)kk * kHeadDim) + lane);
+                    } else {
+                        kv[i] = *reinterpret_cast<const float2*>(kcur + 2 * lane);
+                        vv[i] = *reinterpret_cast<const float2*>(vcur + 2 * lane);
+                    }
                 } else {
                     kv[i] = vv[i] = make_float2(0.f, 0.f);
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) s[i] = fmaf(q.x, kv[i].x, q.y * kv[i].y);
+            for (int i = 0; i < 4; ++i) s4[i] = fmaf(q.x, kv[i].x, q.y * kv[i].y);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], off);
+                for (int i = 0; i < 4; ++i) s4[i] += __shfl_xor_sync(0xffffffffu, s4[i], off);
             float mn = m;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                s[i] = kb + i * kWarps < k1 ? s[i] * 0.125f : -INFINITY;  // rsqrt(64)
-                mn = fmaxf(mn, s[i]);
+                s4[i] = kb + i * kWarps < k1 ? s4[i] * 0.125f : -INFINITY;  // rsqrt(64)
+                mn = fmaxf(mn, s4[i]);
             }
             const float corr = expf(m - mn);
             l *= corr;
@@ -640,7 +718,7 @@ __device__ void phase_attn(Ctx& cx, int li, uint32_t S) {
             o.y *= corr;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float p = expf(s[i] - mn);
+                const float p = expf(s4[i] - mn);
                 l += p;
                 o.x = fmaf(p, vv[i].x, o.x);
                 o.y = fmaf(p, vv[i].y, o.y);
@@ -674,120 +752,163 @@ __device__ void phase_attn(Ctx& cx, int li, uint32_t S) {
         }
         if (c == nch - 1) {
             if (t >= 64 && t < 128)
-                Kc[(size_t)S * kHeadDim + t - 64] = __ldcg(kcur + t - 64);
+                Kc[(size_t)S * kHeadDim + t - 64] = kcur[t - 64];
             else if (t >= 128 && t < 192)
-                Vc[(size_t)S * kHeadDim + t - 128] = __ldcg(vcur + t - 128);
+                Vc[(size_t)S * kHeadDim + t - 128] = vcur[t - 128];
+        }
+        csync();
+        if (t == 0) {
+            unsigned* cnt = &a.b.ctl->head_cnt[li][h];
+            unsigned old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+            const bool last = old == nch - 1;
+            // reused in the next step, after its grid barrier
+            if (last) *reinterpret_cast<volatile unsigned*>(cnt) = 0;
+            cx.sm.last = last;
+        }
+        csync();
+        if (cx.sm.last) {  // last unit of head h: merge its partials
+            if (t < kHeadDim) {
+                const float* ph = a.b.part + (size_t)h * nch * kPartStride;
+                float mv[kMaxChunks], lv[kMaxChunks], ov[kMaxChunks];
+#pragma unroll
+                for (int cc = 0; cc < kMaxChunks; ++cc)
+                    if (cc < (int)nch) {
+                        mv[cc] = __ldcg(ph + cc * kPartStride);
+                        lv[cc] = __ldcg(ph + cc * kPartStride + 1);
+                        ov[cc] = __ldcg(ph + cc * kPartStride + 4 + t);
+                    }
+                float M = -INFINITY;
+#pragma unroll
+                for (int cc = 0; cc < kMaxChunks; ++cc)
+                    if (cc < (int)nch) M = fmaxf(M, mv[cc]);
+                float Ls = 0.f, O = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < kMaxChunks; ++cc)
+                    if (cc < (int)nch) {
+                        const float e = expf(mv[cc] - M);
+                        Ls = fmaf(e, lv[cc], Ls);
+                        O = fmaf(e, ov[cc], O);
+                    }
+                put_tagged(a.b.attn + h * kHeadDim + t, epoch, O / Ls);
+            }
         }
         csync();
     }
+    return true;
 }
 
-__device__ bool phase_oproj(Ctx& cx, int li, uint32_t token, uint32_t pos, uint32_t S) {
+__device__ bool phase_oproj(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
+    int* status = a.b.ctl->status;
     const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0;
     const int t = threadIdx.x;
     float bias = 0.f, res = 0.f;  // used after the last slot
+    bool ok = true;
     if (t < nrows) {
         const int r = r0 + t;
         bias = __ldg(cx.w.layer[li].b_o + r);
-        if (cx.resident)
+        if (cx.resident) {
             res = cx.sm.xin[r];
-        else if (li == 0)  // layered path: the layer input from global memory
+        } else if (li == 0) {  // layered path: the layer input from global memory
             res = __ldg(cx.w.mel_emb + (size_t)token * kWidth + r) + __ldg(cx.w.mel_pos + (size_t)pos * kWidth + r);
-        else
-            res = __ldcg(a.b.h + r);
-    }
-    // merge the split-K attention partials: thread t < 320 produces outputs
-    // 4t..4t+3 (head 4t/64); all loads of its partials are in flight together
-    const uint32_t keys = S + 1;
-    const uint32_t ch = attn_chunk(keys, cx.ncta);
-    const int nch = int((keys + ch - 1) / ch);
-    if (t < kWidth / 4) {
-        const int h = (4 * t) / kHeadDim, d = (4 * t) % kHeadDim;
-        const float* ph = a.b.part + (size_t)h * nch * kPartStride;
-        float2 ml[kMaxChunks];
-        float4 ov[kMaxChunks];
-#pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) {
-            if (c < nch) {
-                ml[c] = __ldcg(reinterpret_cast<const float2*>(ph + c * kPartStride));
-                ov[c] = __ldcg(reinterpret_cast<const float4*>(ph + c * kPartStride + 4 + d));
-            }
+        } else {
+            const unsigned long long* hp = a.b.h + (r & ~1);
+            float v[2];
+            ok = poll_tagged(hp, 1, epoch - 1, v, status, 70 + li);
+            res = v[r & 1];
         }
-        float M = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c)
-            if (c < nch) M = fmaxf(M, ml[c].x);
-        float Ls = 0.f;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) {
-            if (c < nch) {
-                const float e = expf(ml[c].x - M);
-                Ls = fmaf(e, ml[c].y, Ls);
-                o.x = fmaf(e, ov[c].x, o.x);
-                o.y = fmaf(e, ov[c].y, o.y);
-                o.z = fmaf(e, ov[c].z, o.z);
-                o.w = fmaf(e, ov[c].w, o.w);
-            }
-        }
-        *reinterpret_cast<float4*>(&cx.sm.attn[4 * t]) = make_float4(o.x / Ls, o.y / Ls, o.z / Ls, o.w / Ls);
     }
-    csync();
+    ok = ok && stage_tagged(a.b.attn, epoch, cx.sm.attn, status, 70 + li);
+    if (csync_or(!ok)) return false;
     float2 x[kVec];
 #pragma unroll
     for (int j = 0; j < kVec; ++j) x[j] = *reinterpret_cast<const float2*>(&cx.sm.attn[col_of(j)]);
-    float* out = a.b.hm + r0;
-    return gemv_slots(cx, nrows, x, 70 + li, [&](int row, float v) { out[row] = res + (v + bias); });
+    unsigned long long* out = a.b.hm + r0;
+    return gemv_slots(cx, nrows, x, 70 + li, [&](int row, float v) { put_tagged(out + row, epoch, res + (v + bias)); });
 }
 
 // hm -> LN2 -> this CTA's c_fc rows -> GELU -> f.
-__device__ bool phase_fc(Ctx& cx, int li) {
+__device__ bool phase_fc(Ctx& cx, int li, uint32_t epoch) {
     const DecodeArgs& a = cx.a;
     const int f0 = cx.rows.f0, nf = cx.rows.f1 - f0, t = threadIdx.x;
     const float bias = t < nf ? __ldg(cx.w.layer[li].b_fc + f0 + t) : 0.f;
-    stage_vec(a.b.hm, cx.sm.xin);
+    const bool staged = stage_tagged(a.b.hm, epoch, cx.sm.xin, a.b.ctl->status, 100 + li);
     bool abort;
-    const float* slot = ln_slot_wait(cx, abort, 100 + li);
+    const float* slot = ln_slot_wait(cx, staged, abort, 100 + li);
     if (abort) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.f + f0;
-    return gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); });
+    if (!gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); })) return false;
+    // f is read whole by every CTA: one arrival count per layer (monotonic over
+    // the steps of a launch) instead of per-word tags, so readers load it once
+    csync();
+    if (t == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&a.b.ctl->f_cnt[li]) : "memory");
+    return true;
+}
+
+// Thread 0: bounded wait until `*cnt` reaches `target` (acquire); false on
+// timeout or an error status.
+__device__ bool wait_count(const unsigned* cnt, unsigned target, int* status, int where) {
+    if (ld_acquire_gpu(cnt) >= target) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (unsigned spins = 1;; ++spins) {
+        if (ld_acquire_gpu(cnt) >= target) return true;
+        if ((spins & 31u) == 0) {
+            const unsigned long long dt = globaltimer_ns() - t0;
+            if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
+            if (dt > kWaitLimitNs) {
+                set_status(status, kStatusBarrierTimeout, where, (int)target);
+                return false;
+            }
+        }
+    }
 }
 
 // f -> this CTA's mlp.c_proj rows (the rows of its attn.c_proj block) -> h = hm + y + bias.
-__device__ bool phase_mp(Ctx& cx, int li) {
+__device__ bool phase_mp(Ctx& cx, int li, uint32_t epoch) {
     const DecodeArgs& a = cx.a;
+    int* status = a.b.ctl->status;
     const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0, t = threadIdx.x;
     float bias = 0.f, res = 0.f;
+    bool ok = true;
     if (t < nrows) {
         bias = __ldg(cx.w.layer[li].b_mp + r0 + t);
-        res = __ldcg(a.b.hm + r0 + t);
+        float v[2];
+        ok = poll_tagged(a.b.hm + ((r0 + t) & ~1), 1, epoch, v, status, 160 + li);
+        res = v[(r0 + t) & 1];
     }
+    if (t == 0) {
+        const unsigned step = (epoch - 1) / unsigned(cx.w.layers);
+        ok = wait_count(&a.b.ctl->f_cnt[li], unsigned(cx.ncta) * (step + 1), status, 160 + li) && ok;
+    }
+    if (csync_or(!ok)) return false;
     float2 x[kVec];
 #pragma unroll
     for (int j = 0; j < kVec; ++j) x[j] = __ldcg(reinterpret_cast<const float2*>(a.b.f + long_col_of(j)));
-    float* out = a.b.h + r0;
-    return gemv_long_slots(cx, nrows, x, 160 + li, [&](int row, float v) { out[row] = res + (v + bias); });
+    unsigned long long* out = a.b.h + r0;
+    return gemv_long_slots(cx, nrows, x, 160 + li,
+                           [&](int row, float v) { put_tagged(out + row, epoch, res + (v + bias)); });
 }
 
 // gpt.cpp:120-122: last hidden row -> ln_f -> final_norm -> mel_head.
-__device__ bool phase_head(Ctx& cx, uint32_t token, uint32_t pos) {
+// `epoch` is that of the last layer (whose output h is the input).
+__device__ bool phase_head(Ctx& cx, uint32_t epoch, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.h0, nrows = cx.rows.h1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.b_head + r0 + t) : 0.f;
-    stage_resid(a, cx.w, cx.w.layers, token, pos, cx.sm.xin);
+    const bool staged = stage_resid(a, cx.w, cx.w.layers, epoch + 1, token, pos, cx.sm.xin, 200);
     bool abort;
-    const float* slot = ln_slot_wait(cx, abort, 200);
+    const float* slot = ln_slot_wait(cx, staged, abort, 200);
     if (abort) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
-    slot = ln_slot_wait(cx, abort, 200);
+    slot = ln_slot_wait(cx, true, abort, 200);
     if (abort) return false;
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
@@ -831,20 +952,20 @@ __device__ bool grid_barrier(Ctx& cx, unsigned& target, int where) {
     return cx.sm.abort != 0;
 }
 
-// One forward step; true when aborted.  Five grid barriers per layer: after
-// the QKV rows, the attention partials, the residual after attention, the
-// GELU outputs and the layer output.
-__device__ bool forward_step(Ctx& cx, uint32_t token, uint32_t pos, uint32_t S, unsigned& target) {
+// One forward step (number `step` of the launch); true when aborted.  The
+// layers hand their activations on as tagged words; the step's one grid
+// barrier follows the head (the sampler needs every CTA's logits, and the
+// barrier also publishes this step's K/V appends to the next step).
+__device__ bool forward_step(Ctx& cx, int step, uint32_t token, uint32_t pos, uint32_t S, unsigned& target) {
     const int L = cx.w.layers;
+    const uint32_t e0 = uint32_t(step) * uint32_t(L);
     for (int li = 0; li < L; ++li) {
-        if (!phase_qkv(cx, li, token, pos) || grid_barrier(cx, target, li * 8 + 0)) return true;
-        phase_attn(cx, li, S);
-        if (grid_barrier(cx, target, li * 8 + 1)) return true;
-        if (!phase_oproj(cx, li, token, pos, S) || grid_barrier(cx, target, li * 8 + 2)) return true;
-        if (!phase_fc(cx, li) || grid_barrier(cx, target, li * 8 + 3)) return true;
-        if (!phase_mp(cx, li) || grid_barrier(cx, target, li * 8 + 4)) return true;
+        const uint32_t e = e0 + li + 1;
+        if (!phase_qkv(cx, li, e, token, pos) || !phase_attn(cx, li, e, S) || !phase_oproj(cx, li, e, token, pos) ||
+            !phase_fc(cx, li, e) || !phase_mp(cx, li, e))
+            return true;
     }
-    return !phase_head(cx, token, pos) || grid_barrier(cx, target, 1000);
+    return !phase_head(cx, e0 + L, token, pos) || grid_barrier(cx, target, 1000);
 }
 
 // The sampler in its own frame, so its registers do not constrain the phases.
@@ -895,7 +1016,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
             sampler_mark_seen(sm.sa, token);
             if (i + 1 == a.n_iter) break;
         }
-        if (forward_step(cx, token, a.pos0 + i, a.s0 + i, target)) break;
+        if (forward_step(cx, int(i), token, a.pos0 + i, a.s0 + i, target)) break;
         ++fwd;
     }
     if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
@@ -913,8 +1034,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
 // ------------------------------------------------------------ layered path
 enum LayerPhase : int { kPhQkv = 0, kPhAttn, kPhOproj, kPhFc, kPhMp, kPhHead };
 
-__global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phase, int li, uint32_t pos,
-                                                          uint32_t S) {
+__global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phase, int li, uint32_t epoch,
+                                                          uint32_t pos, uint32_t S) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
     if (ld_volatile(&a.b.ctl->done)) return;
@@ -940,12 +1061,12 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phas
     const uint32_t token = *reinterpret_cast<volatile uint32_t*>(&a.b.ctl->token);
     Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, false};
     switch (phase) {
-        case kPhQkv: phase_qkv(cx, li, token, pos); break;
-        case kPhAttn: phase_attn(cx, li, S); break;
-        case kPhOproj: phase_oproj(cx, li, token, pos, S); break;
-        case kPhFc: phase_fc(cx, li); break;
-        case kPhMp: phase_mp(cx, li); break;
-        default: phase_head(cx, token, pos); break;
+        case kPhQkv: phase_qkv(cx, li, epoch, token, pos); break;
+        case kPhAttn: phase_attn(cx, li, epoch, S); break;
+        case kPhOproj: phase_oproj(cx, li, epoch, token, pos); break;
+        case kPhFc: phase_fc(cx, li, epoch); break;
+        case kPhMp: phase_mp(cx, li, epoch); break;
+        default: phase_head(cx, epoch, token, pos); break;
     }
     if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
 }
@@ -1084,12 +1205,14 @@ cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cud
         if (a.mode == kModeGenerate && i + 1 == a.n_iter) break;
         const uint32_t pos = a.pos0 + i, S = a.s0 + i;
         for (int l = 0; l < layers; ++l) {
+            const uint32_t epoch = i * uint32_t(layers) + uint32_t(l) + 1;
             for (int ph = kPhQkv; ph <= kPhMp; ++ph) {
-                k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, ph, l, pos, S);
+                k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, ph, l, epoch, pos, S);
                 ++*launches;
             }
         }
-        k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, layers, pos, S);
+        k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, layers, i * uint32_t(layers) + uint32_t(layers),
+                                                              pos, S);
         ++*launches;
     }
     k_layer_finish<<<1, 1, 0, s>>>(a);
@@ -1098,7 +1221,7 @@ cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cud
 }
 
 cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s) {
-    k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, 0, 0, 0);
+    k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, 0, 0, 0, 0);
     return cudaGetLastError();
 }
 

@@ -95,6 +95,7 @@ struct itts_gpt_ctx {
     uint32_t* d_codes = nullptr;    // [kCap]
     uint32_t* d_info = nullptr;     // [4]
     float* d_misc = nullptr;        // prepare inputs / processor buffers
+    size_t tagged_bytes = 0;        // bytes of the tagged hand-off region (db.qkv ...)
     uint32_t* d_hist = nullptr;     // processor history (grown on demand)
     size_t d_hist_cap = 0;
     float* d_beam = nullptr;        // beam logits slots + scores
@@ -307,27 +308,29 @@ void alloc_buffers(itts_gpt_ctx* c) {
     c->d_r = c->d_att + T * kW;
     c->d_qkv = c->d_r + T * kW;
     c->d_ff = c->d_qkv + T * 3840;
-    // decode activations (each region 256-byte aligned): qkv, h, hm, f, logits,
-    // attention partials, control block
-    const size_t sizes[7] = {3840 * 4, kW * 4, kW * 4, 5120 * 4, 8448 * 4, size_t(kH) * 256 * 68 * 4,
+    // decode activations (each region 256-byte aligned): the tagged hand-off
+    // words (qkv, h, hm, attn, f), logits, attention partials, control block
+    const size_t sizes[8] = {3840 * 8, kW * 8, kW * 8, kW * 8, 5120 * 8, 8448 * 4, size_t(kH) * 256 * 68 * 4,
                              sizeof(itts::DecodeCtl)};
     size_t total = 0;
     for (size_t s : sizes) total += align256(s);
     c->d_act = reinterpret_cast<float*>(dev_alloc<char>(total, "decode buffers"));
     char* p = reinterpret_cast<char*>(c->d_act);
-    char* regions[7];
-    for (int i = 0; i < 7; ++i) {
+    char* regions[8];
+    for (int i = 0; i < 8; ++i) {
         regions[i] = p;
         p += align256(sizes[i]);
     }
+    c->tagged_bytes = size_t(regions[5] - regions[0]);
     c->db.kv = c->d_kv;
-    c->db.qkv = reinterpret_cast<float*>(regions[0]);
-    c->db.h = reinterpret_cast<float*>(regions[1]);
-    c->db.hm = reinterpret_cast<float*>(regions[2]);
-    c->db.f = reinterpret_cast<float*>(regions[3]);
-    c->db.logits = reinterpret_cast<float*>(regions[4]);
-    c->db.part = reinterpret_cast<float*>(regions[5]);
-    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[6]);
+    c->db.qkv = reinterpret_cast<unsigned long long*>(regions[0]);
+    c->db.h = reinterpret_cast<unsigned long long*>(regions[1]);
+    c->db.hm = reinterpret_cast<unsigned long long*>(regions[2]);
+    c->db.attn = reinterpret_cast<unsigned long long*>(regions[3]);
+    c->db.f = reinterpret_cast<float*>(regions[4]);
+    c->db.logits = reinterpret_cast<float*>(regions[5]);
+    c->db.part = reinterpret_cast<float*>(regions[6]);
+    c->db.ctl = reinterpret_cast<itts::DecodeCtl*>(regions[7]);
     c->db.sampler_big = reinterpret_cast<itts::SamplerBig*>(
         dev_alloc<char>(size_t(c->sm_count) * itts::sampler_big_bytes(), "sampler workspace"));
     c->d_sampler_big = c->db.sampler_big;
@@ -388,6 +391,8 @@ itts::DecodeArgs decode_args(itts_gpt_ctx* c) {
 
 void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     reset_ctl(c);
+    // epochs restart at 1 in every launch: clear the tagged hand-off words
+    ck(cudaMemsetAsync(c->db.qkv, 0, c->tagged_bytes, c->stream), "hand-off reset");
     if (c->mode == 0) {
         ck(itts::launch_decode_persistent(a, c->sm_count, c->stream), "persistent decode launch");
         ++c->launches;

@@ -62,7 +62,8 @@ struct DecodeCtl {
     int status[4];       // {code, where, cta, detail}
     uint32_t info[4];    // {n_codes, stopped, status, forward_steps}
     unsigned bar;        // grid-barrier arrival counter (monotonic per launch)
-    unsigned head_cnt[20];  // split-K attention arrival counters per head
+    unsigned head_cnt[24][20];  // split-K attention arrivals per (layer, head); the last resets it
+    unsigned f_cnt[24];         // CTAs that published their GELU outputs, per layer (all steps)
     uint32_t token;      // current code (layered mode)
     int done;            // layered mode: loop finished
     unsigned pad[5];
@@ -73,10 +74,14 @@ struct SamplerBig;
 // Decode-time device buffers (activations live in L2; KV cache in HBM).
 struct DecodeBuffers {
     float* kv;        // [layer][K|V][head][4096][64] fp32
-    float* qkv;       // [3840]
-    float* h;         // [1280] residual stream leaving the last finished layer
-    float* hm;        // [1280] residual stream after the attention block
-    float* f;         // [5120] GELU(c_fc) of the current layer
+    // Activations handed between CTAs as tagged words: (epoch << 32) | float
+    // bits, written once per layer; a reader polls until every word it needs
+    // carries the epoch of the layer it wants (zeroed before each launch).
+    unsigned long long* qkv;   // [3840]
+    unsigned long long* h;     // [1280] residual stream leaving a layer
+    unsigned long long* hm;    // [1280] residual stream after the attention block
+    unsigned long long* attn;  // [1280] merged attention output
+    float* f;                  // [5120] GELU(c_fc), published by DecodeCtl::f_cnt
     float* logits;    // [8194]
     float* part;      // split-K attention partials [20 * 256 * 68]
     SamplerBig* sampler_big;  // one large-survivor workspace per CTA
