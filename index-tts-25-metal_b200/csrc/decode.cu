@@ -448,21 +448,30 @@ __device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool staged, bool&
     return slot;
 }
 
-constexpr int kMaxSlotsPerPhase = 8;  // 64 rows of 1280 or 16 rows of 5120 per CTA
+// Slots per phase and CTA for grids of 129..148 CTAs (the host requires
+// ceil(8194 / grid) <= 64): c_attn 30 rows, c_proj 10, c_fc 40, mlp.c_proj 10
+// long rows, mel_head 64 rows.  The slot loop of each phase is unrolled to
+// exactly its bound, which keeps the kernel's code (and its instruction-cache
+// footprint per layer) small.
+constexpr int kSlotsQkv = (30 + kRowsPerSlot - 1) / kRowsPerSlot;
+constexpr int kSlotsO = (10 + kRowsPerSlot - 1) / kRowsPerSlot;
+constexpr int kSlotsFc = (40 + kRowsPerSlot - 1) / kRowsPerSlot;
+constexpr int kSlotsMp = (10 + kLongPerSlot - 1) / kLongPerSlot;
+constexpr int kSlotsHead = (64 + kRowsPerSlot - 1) / kRowsPerSlot;
 
 // Dot products of x with `nrows` streamed rows of kRowLen floats (kRowsPer
 // per slot, kWPR warps per row).  Each warp keeps one partial per slot in a
 // register and the butterflies of all slots run together after the last one,
 // so a slot costs its wait, loads, FMAs and release; block sums go to
 // red[row * kWPR + block].
-template <int kRowLen, int kRowsPer, int kWPR>
+template <int kRowLen, int kRowsPer, int kWPR, int kMaxSlots>
 __device__ bool stream_dots(Ctx& cx, int nrows, const float2 (&x)[kVec], float* red, int where) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rr = warp / kWPR, q = warp % kWPR;
-    float acc[kMaxSlotsPerPhase];
+    float acc[kMaxSlots];
     bool ok = true;
 #pragma unroll
-    for (int si = 0; si < kMaxSlotsPerPhase; ++si) {
+    for (int si = 0; si < kMaxSlots; ++si) {
         acc[si] = 0.f;
         const int r0 = si * kRowsPer;
         if (r0 < nrows && ok) {
@@ -486,10 +495,10 @@ __device__ bool stream_dots(Ctx& cx, int nrows, const float2 (&x)[kVec], float* 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int si = 0; si < kMaxSlotsPerPhase; ++si) acc[si] += __shfl_xor_sync(0xffffffffu, acc[si], o);
+        for (int si = 0; si < kMaxSlots; ++si) acc[si] += __shfl_xor_sync(0xffffffffu, acc[si], o);
     if (lane == 0)
 #pragma unroll
-        for (int si = 0; si < kMaxSlotsPerPhase; ++si) {
+        for (int si = 0; si < kMaxSlots; ++si) {
             const int r = si * kRowsPer + rr;
             if (r < nrows) red[r * kWPR + q] = acc[si];
         }
@@ -498,9 +507,9 @@ __device__ bool stream_dots(Ctx& cx, int nrows, const float2 (&x)[kVec], float* 
 
 // y[row] = W[row, :] . x for `nrows` streamed 1280-wide rows; epi(row, y)
 // runs on consumer thread `row` once all slots are consumed.
-template <class Epi>
+template <int kMaxSlots, class Epi>
 __device__ bool gemv_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
-    const bool ok = stream_dots<kWidth, kRowsPerSlot, kWarpsPerRow>(cx, nrows, x, &cx.sm.rowred[0][0], where);
+    const bool ok = stream_dots<kWidth, kRowsPerSlot, kWarpsPerRow, kMaxSlots>(cx, nrows, x, &cx.sm.rowred[0][0], where);
     if (csync_or(!ok)) return false;
     const int t = threadIdx.x;
     if (t < nrows) {
@@ -607,7 +616,7 @@ __device__ __forceinline__ int long_col_of(int j) {
 // per slot); epi(row, y) runs on thread `row` once all slots are consumed.
 template <class Epi>
 __device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int where, Epi epi) {
-    const bool ok = stream_dots<kFfn, kLongPerSlot, kWarpsPerLong>(cx, nrows, x, &cx.sm.longred[0][0], where);
+    const bool ok = stream_dots<kFfn, kLongPerSlot, kWarpsPerLong, kSlotsMp>(cx, nrows, x, &cx.sm.longred[0][0], where);
     if (csync_or(!ok)) return false;
     const int t = threadIdx.x;
     if (t < nrows) {
@@ -638,7 +647,7 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint3
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     unsigned long long* out = a.b.qkv + r0;
-    return gemv_slots(cx, nrows, x, 40 + li, [&](int row, float v) { put_tagged(out + row, epoch, v + bias); });
+    return gemv_slots<kSlotsQkv>(cx, nrows, x, 40 + li, [&](int row, float v) { put_tagged(out + row, epoch, v + bias); });
 }
 
 // Key chunk of one attention unit: a multiple of 16 keys, at most kMaxChunks
@@ -825,7 +834,8 @@ __device__ bool phase_oproj(Ctx& cx, int li, uint32_t epoch, uint32_t token, uin
 #pragma unroll
     for (int j = 0; j < kVec; ++j) x[j] = *reinterpret_cast<const float2*>(&cx.sm.attn[col_of(j)]);
     unsigned long long* out = a.b.hm + r0;
-    return gemv_slots(cx, nrows, x, 70 + li, [&](int row, float v) { put_tagged(out + row, epoch, res + (v + bias)); });
+    return gemv_slots<kSlotsO>(cx, nrows, x, 70 + li,
+                               [&](int row, float v) { put_tagged(out + row, epoch, res + (v + bias)); });
 }
 
 // hm -> LN2 -> this CTA's c_fc rows -> GELU -> f.
@@ -842,7 +852,8 @@ __device__ bool phase_fc(Ctx& cx, int li, uint32_t epoch) {
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.f + f0;
-    if (!gemv_slots(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); })) return false;
+    if (!gemv_slots<kSlotsFc>(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); }))
+        return false;
     // f is read whole by every CTA: one arrival count per layer (monotonic over
     // the steps of a launch) instead of per-word tags, so readers load it once
     csync();
@@ -913,7 +924,7 @@ __device__ bool phase_head(Ctx& cx, uint32_t epoch, uint32_t token, uint32_t pos
     layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
     slot_release(cx);
     float* out = a.b.logits + r0;
-    return gemv_slots(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
+    return gemv_slots<kSlotsHead>(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
 }
 
 // Grid barrier of the persistent kernel (all CTAs co-resident by the
