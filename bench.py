@@ -234,7 +234,8 @@ def run_ours(args):
                         rng=gpt.RNG_PHILOX)
     stream = torch.cuda.ExternalStream(dec.stream, device=local)
     d_prefix = torch.from_numpy(prefix).to(f"cuda:{local}")
-    d_codes = torch.zeros(N_CODES, dtype=torch.int32, device=f"cuda:{local}")
+    n_codes = args.codes
+    d_codes = torch.zeros(n_codes, dtype=torch.int32, device=f"cuda:{local}")
     d_info = torch.zeros(4, dtype=torch.int32, device=f"cuda:{local}")
     torch.cuda.synchronize()
 
@@ -256,7 +257,7 @@ def run_ours(args):
         dec.prefill_async(d_prefix.data_ptr(), rows)
         if ev:
             ev[1].record(stream)
-        dec.decode_async(opts, N_CODES, d_codes.data_ptr(), d_info.data_ptr())
+        dec.decode_async(opts, n_codes, d_codes.data_ptr(), d_info.data_ptr())
         if ev:
             ev[2].record(stream)
 
@@ -285,29 +286,34 @@ def run_ours(args):
     info_h = d_info.cpu().numpy()
     fwd = int(info_h[3])
     elapsed_max = max_over_ranks(elapsed_ms)
-    tokens = world * args.steps * N_CODES
+    tokens = world * args.steps * n_codes
     value = tokens / (elapsed_max / 1000.0)
 
     # ---- public API with host buffers (e2e)
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        r = dec.generate(prefix, opts, N_CODES)
+        r = dec.generate(prefix, opts, n_codes)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    assert len(r.codes) == N_CODES
-    e2e_value = world * args.steps * N_CODES / e2e_s
+    assert len(r.codes) == n_codes
+    e2e_value = world * args.steps * n_codes / e2e_s
 
     pk, pk_kind = peaks()
     alg = decode_bytes(info.stream_bytes, info.layers, rows, fwd)
     avg_decode_s = statistics.mean(decode_ms) / 1000.0
     achieved = alg / avg_decode_s / 1e9
     peak_gbs = float(pk["hbm_gbs"])
+    # DRAM traffic of the decode kernel: the ratio of DRAM bytes (ncu,
+    # dram__bytes_read.sum + dram__bytes_write.sum) to algorithmic bytes of a
+    # small captured launch, applied to this launch's algorithmic bytes
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+            tj = json.load(f)
+        if tj.get("capture_dram_bytes") and tj.get("capture_algorithmic_bytes"):
+            traffic = alg * tj["capture_dram_bytes"] / tj["capture_algorithmic_bytes"]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -321,14 +327,14 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, seeded conditioning latents and text ids)",
             "config": {"workload": "configs[1]: sampled decode (T 0.8, top-k 30, top-p 0.8, rp 10, Philox "
-                                   "seed 1234), prefix 32 latents + 200 text tokens, 1024 codes, batch 1",
+                                   f"seed 1234), prefix 32 latents + 200 text tokens, {n_codes} codes, batch 1",
                        "model": "UnifiedVoice GPT 24L d1280 H20 FFN5120 fp32 random-init (seed 42)",
-                       "global_batch": world, "prefix_rows": rows, "codes_per_request": N_CODES,
+                       "global_batch": world, "prefix_rows": rows, "codes_per_request": n_codes,
                        "parallelism": f"replicas x{world} (one request per GPU, no collective)",
                        "l2": "inputs larger than L2: each forward step streams 1.93 GB of weights (L2 126 MB)",
                        "decode_mode": "persistent cooperative kernel"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(prefix.nbytes),
-                    "d2h_bytes_per_step": int(N_CODES * 4 + 48)},
+                    "d2h_bytes_per_step": int(n_codes * 4 + 48)},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "traffic": traffic,
@@ -355,6 +361,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--codes", type=int, default=N_CODES,
+                    help="codes per request (1024 is the benchmark; smaller values are for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
