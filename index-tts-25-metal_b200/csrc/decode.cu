@@ -1,36 +1,32 @@
 // Batch-1 decode of the IndexTTS 2.5 GPT on B200 (sm_100a).
 //
-// One decode step (src/gpt.cpp:88-125 with initial=false) is four phases per
+// One decode step (src/gpt.cpp:88-125 with initial=false) is five phases per
 // layer plus the head, each a function of (cta, ncta) over the whole grid:
-//   A    h -> LN1 -> QKV GEMV (rows of [3840 x 1280])
-//   B    split-K attention over the KV cache + K/V append (kernels.metal:2064-2145)
-//   C    merge of the attention partials -> c_proj GEMV + bias + residual -> r
-//   MLP  r -> LN2 -> c_fc GEMV + GELU (this CTA's 5120/ncta rows) -> their share
-//        of mlp.c_proj as a split-K product over those rows (mlp.c_proj kept
-//        in its [in, out] layout), summed across CTAs with 64-bit fixed-point
-//        atomics (order independent, hence deterministic)
-//   head ln_f -> final_norm -> mel_head GEMV
-// The next layer's h = r + (mlp + bias) is rebuilt from r and the fixed-point
-// sums by every CTA that needs it, so the step has 4 grid-wide dependencies per
-// layer instead of 6.
+//   A    h -> LN1 -> this CTA's c_attn rows -> qkv
+//   B    split-K attention over the KV cache + K/V append (kernels.metal:2064-
+//        2145); the last unit of each head merges the head's partials -> attn
+//   C    attn -> this CTA's attn.c_proj rows + bias + residual -> hm
+//   D    hm -> LN2 -> this CTA's c_fc rows + GELU -> f
+//   E    f -> this CTA's mlp.c_proj rows (5120 wide) + bias + residual -> h
+//   head h -> ln_f -> final_norm -> mel_head rows -> logits
+// Activations pass between CTAs as epoch-tagged 64-bit words that the reader
+// polls (the data is its own flag), f through a per-layer arrival counter; the
+// only grid barrier of a step follows the head.
 //
 // Weight streaming: every CTA owns a contiguous block of rows per matrix.  Its
-// rows (and the LayerNorm vectors) are fetched into a 10-slot x 20 KB shared-
-// memory ring with cp.async.bulk (1-D TMA, completion on a "full" mbarrier;
-// no multicast) by a dedicated producer warp that runs up to ten slots ahead of
-// the 16 consumer warps (a consumed slot is handed back on an "empty"
-// mbarrier) and issues cp.async.bulk.prefetch.L2 ten slots further ahead.  The
-// stream therefore runs through grid barriers, the attention phase and the
-// sampler, which are the latency-bound parts of the step; the consumers read
-// weights from shared memory and synchronise on a named barrier the producer
-// never joins.  Attention reads K/V directly (L2-coherent loads): one warp per key
-// subset with an online softmax, K and V fetched together.
+// rows (and the LayerNorm packs) are fetched into a 5-slot x 40 KB shared-
+// memory ring with cp.async.bulk (1-D TMA, completion on a "full" mbarrier,
+// L2 evict-first; no multicast) by a dedicated producer warp that walks the
+// CTA's segment schedule; the 16 consumer warps hand a slot back on its
+// "empty" mbarrier, and while the ring is full the producer prefetches further
+// ahead into L2.  The stream therefore runs through the hand-off waits, the
+// attention phase and the sampler, which are the latency-bound parts of the
+// step.
 //
 // Drivers:
-//   * k_decode: one cooperative launch (one 512-thread CTA per SM) for a whole
-//     token loop; grid barriers (bounded spin on an L2 counter) between phases;
-//     the sampler runs redundantly in every CTA so the next token needs no
-//     extra barrier.
+//   * k_decode: one cooperative launch (one CTA per SM) for a whole token
+//     loop; the sampler runs redundantly in every CTA so the next token needs
+//     no extra barrier.
 //   * k_phase: one launch per phase with the same device code (layered mode,
 //     for diagnosis and as the non-cooperative path); its ring covers only that
 //     phase.
