@@ -285,9 +285,10 @@ def run_ours(args):
     prefill_ms = [e[0].elapsed_time(e[1]) for e in evs]
     info_h = d_info.cpu().numpy()
     fwd = int(info_h[3])
-    elapsed_max = max_over_ranks(elapsed_ms)
-    tokens = world * args.steps * n_codes
-    value = tokens / (elapsed_max / 1000.0)
+    replicas = importlib.import_module("index-tts-25-metal_b200.replicas")
+    agg = replicas.aggregate(args.steps * n_codes, elapsed_ms / 1000.0, device=f"cuda:{local}")
+    elapsed_max = 1000.0 * agg["seconds"]
+    value = agg["value"]  # all ranks' codes / the slowest rank's device time
 
     # ---- public API with host buffers (e2e)
     barrier()
