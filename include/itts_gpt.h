@@ -131,6 +131,19 @@ int itts_gpt_step(itts_gpt_ctx* ctx, uint32_t code, uint32_t position, float* lo
 int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const itts_gen_opts* opts,
                       uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes, int* stopped);
 
+/* ---- batch of independent requests ----------------------------------------
+ * Request i is the prefix prefixes[i] (n_floats[i] floats) with options
+ * opts[i]; each is prefilled and decoded exactly as itts_gpt_generate would,
+ * one after another on the context's device.  Codes of request i go to
+ * codes + i * max_tokens, its count to n_codes[i], its stop flag to
+ * stopped[i].  Every request is validated before any runs.  No single call
+ * of the reference corresponds: its server runs GptDecoder::generate once per
+ * request (src/server.cpp:41-47); this is that loop behind one call.  The
+ * context's cache holds the last request's state afterwards. */
+int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const* prefixes, const size_t* n_floats,
+                            const itts_gen_opts* opts, uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes,
+                            int* stopped);
+
 /* ---- GptDecoder::checkpoint / restore / cached_tokens (gpt.cpp:86-87) ----- */
 int itts_gpt_checkpoint(itts_gpt_ctx* ctx, itts_gpt_state** out);
 int itts_gpt_restore(itts_gpt_ctx* ctx, const itts_gpt_state* state);

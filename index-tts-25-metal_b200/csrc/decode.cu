@@ -630,7 +630,35 @@ __device__ bool gemv_long_slots(Ctx& cx, int nrows, const float2 (&x)[kVec], int
 }
 
 // ---------------------------------------------------------------- phases
-__device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint32_t pos) {
+// Key chunk of one attention unit: a multiple of 16 keys, at most kMaxChunks
+// chunks per head, about one unit per CTA.
+__device__ __forceinline__ uint32_t attn_chunk(uint32_t keys, int ncta) {
+    uint32_t ch = (keys * kHeads + ncta - 1) / ncta;
+    ch = max(ch, (keys + kMaxChunks - 1) / kMaxChunks);
+    return max((ch + 15u) & ~15u, 16u);
+}
+
+// Thread 0: starts fetching the cached K/V rows of this CTA's attention units
+// (keys [k0, min(k1, S)) of phase B, written in earlier steps) into L2 while
+// phase A runs, so phase B's loads hit L2.
+__device__ __forceinline__ void prefetch_attn_kv(const Ctx& cx, int li, uint32_t S) {
+    const uint32_t keys = S + 1;
+    const uint32_t ch = attn_chunk(keys, cx.ncta);
+    const uint32_t nch = (keys + ch - 1) / ch, units = kHeads * nch;
+    for (uint32_t u = cx.cta; u < units; u += cx.ncta) {
+        const uint32_t h = u / nch, k0 = (u % nch) * ch, k1 = min(k0 + ch, S);
+        if (k1 <= k0) continue;
+        const uint32_t bytes = (k1 - k0) * kHeadDim * 4;
+        for (int kv = 0; kv < 2; ++kv) {
+            const float* src = cx.a.b.kv + (((size_t)li * 2 + kv) * kHeads + h) * (size_t)kKvCapacity * kHeadDim +
+                               (size_t)k0 * kHeadDim;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+        }
+    }
+}
+
+__device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint32_t pos, uint32_t S) {
+    if (threadIdx.x == 0) prefetch_attn_kv(cx, li, S);
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.q0, nrows = cx.rows.q1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.layer[li].b_qkv + r0 + t) : 0.f;  // used after the last slot
@@ -644,14 +672,6 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint3
     slot_release(cx);
     unsigned long long* out = a.b.qkv + r0;
     return gemv_slots<kSlotsQkv>(cx, nrows, x, 40 + li, [&](int row, float v) { put_tagged(out + row, epoch, v + bias); });
-}
-
-// Key chunk of one attention unit: a multiple of 16 keys, at most kMaxChunks
-// chunks per head, about one unit per CTA.
-__device__ __forceinline__ uint32_t attn_chunk(uint32_t keys, int ncta) {
-    uint32_t ch = (keys * kHeads + ncta - 1) / ncta;
-    ch = max(ch, (keys + kMaxChunks - 1) / kMaxChunks);
-    return max((ch + 15u) & ~15u, 16u);
 }
 
 // Split-K attention for the current query over keys [0, S] (S cached + the
@@ -968,7 +988,7 @@ __device__ bool forward_step(Ctx& cx, int step, uint32_t token, uint32_t pos, ui
     const uint32_t e0 = uint32_t(step) * uint32_t(L);
     for (int li = 0; li < L; ++li) {
         const uint32_t e = e0 + li + 1;
-        if (!phase_qkv(cx, li, e, token, pos) || !phase_attn(cx, li, e, S) || !phase_oproj(cx, li, e, token, pos) ||
+        if (!phase_qkv(cx, li, e, token, pos, S) || !phase_attn(cx, li, e, S) || !phase_oproj(cx, li, e, token, pos) ||
             !phase_fc(cx, li, e) || !phase_mp(cx, li, e))
             return true;
     }
@@ -976,8 +996,9 @@ __device__ bool forward_step(Ctx& cx, int step, uint32_t token, uint32_t pos, ui
 }
 
 // The sampler in its own frame, so its registers do not constrain the phases.
-__device__ __noinline__ uint32_t sample_next(const DecodeArgs& a, uint32_t i, SamplerSmem& sa, SamplerBig* big) {
-    return run_sampler(a.b.logits, a.opts, i, a.opts.do_sample == 0, sa, big, nullptr, a.b.ctl->status);
+__device__ __noinline__ uint32_t sample_next(const float* logits, SampleOpts o, uint32_t i, SamplerSmem& sa,
+                                             SamplerBig* big, int* status) {
+    return run_sampler(logits, o, i, o.do_sample == 0, sa, big, nullptr, status);
 }
 
 constexpr int kCtaThreads = kThreads + 32;  // 16 consumer warps + the producer warp
@@ -1008,7 +1029,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
     uint32_t token = a.first_code, n_codes = 0, stopped = 0, fwd = 0;
     for (uint32_t i = 0; i < a.n_iter; ++i) {
         if (a.mode == kModeGenerate) {
-            token = sample_next(a, i, sm.sa, big);
+            token = sample_next(a.b.logits, a.opts, i, sm.sa, big, a.b.ctl->status);
             if (token == (uint32_t)kStopCode) {
                 stopped = 1;
                 break;
@@ -1068,7 +1089,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phas
     const uint32_t token = *reinterpret_cast<volatile uint32_t*>(&a.b.ctl->token);
     Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, false};
     switch (phase) {
-        case kPhQkv: phase_qkv(cx, li, epoch, token, pos); break;
+        case kPhQkv: phase_qkv(cx, li, epoch, token, pos, S); break;
         case kPhAttn: phase_attn(cx, li, epoch, S); break;
         case kPhOproj: phase_oproj(cx, li, epoch, token, pos); break;
         case kPhFc: phase_fc(cx, li, epoch); break;

@@ -814,6 +814,36 @@ int itts_gpt_step(itts_gpt_ctx* ctx, uint32_t code, uint32_t position, float* lo
     });
 }
 
+// One request of generate / generate_batch (gpt_sampling.cpp:168-189; beams
+// :190-245); options already validated into `o`.
+void generate_one(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const itts::SampleOpts& o, float lp,
+                  uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes, int* stopped) {
+    if (o.num_beams > 1) {
+        bool eos = false;
+        auto r = beam_search(ctx, prefix, n_floats, o, lp, max_tokens, eos);
+        std::memcpy(codes, r.data(), r.size() * 4);
+        *n_codes = uint32_t(r.size());
+        *stopped = eos ? 1 : 0;
+        return;
+    }
+    host_prefill(ctx, prefix, n_floats);
+    itts::DecodeArgs a = decode_args(ctx);
+    a.mode = itts::kModeGenerate;
+    a.n_iter = max_tokens;
+    a.s0 = ctx->cached;
+    a.pos0 = 2;  // first generated code sits at mel position 2 (gpt_sampling.cpp:184-186)
+    a.opts = o;
+    launch_decode(ctx, a);
+    ck(cudaMemcpyAsync(ctx->h_codes, ctx->d_codes, size_t(max_tokens) * 4, cudaMemcpyDeviceToHost, ctx->stream),
+       "codes read");
+    check_status(ctx);
+    const itts::DecodeCtl& ctl = *ctx->h_ctl;
+    ctx->cached += ctl.info[3];
+    *n_codes = ctl.info[0];
+    *stopped = int(ctl.info[1]);
+    std::memcpy(codes, ctx->h_codes, size_t(ctl.info[0]) * 4);
+}
+
 int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const itts_gen_opts* opts,
                       uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes, int* stopped) {
     if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
@@ -823,30 +853,28 @@ int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, c
         validate_capacity(ctx, n_floats / kW, max_tokens);
         float lp = 0;
         const itts::SampleOpts o = configure(*opts, &lp);
-        if (o.num_beams > 1) {
-            bool eos = false;
-            auto r = beam_search(ctx, prefix, n_floats, o, lp, max_tokens, eos);
-            std::memcpy(codes, r.data(), r.size() * 4);
-            *n_codes = uint32_t(r.size());
-            *stopped = eos ? 1 : 0;
-            return;
+        generate_one(ctx, prefix, n_floats, o, lp, max_tokens, codes, n_codes, stopped);
+    });
+}
+
+int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const* prefixes, const size_t* n_floats,
+                            const itts_gen_opts* opts, uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes,
+                            int* stopped) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (batch == 0) return;
+        if (!prefixes || !n_floats || !opts || !codes || !n_codes || !stopped) invalid("null batch argument");
+        std::vector<itts::SampleOpts> o(batch);
+        std::vector<float> lp(batch, 0.f);
+        for (size_t i = 0; i < batch; ++i) {  // every request is checked before any runs
+            if (!prefixes[i]) invalid("null prefix in batch");
+            validate_capacity(ctx, n_floats[i] / kW, max_tokens);
+            o[i] = configure(opts[i], &lp[i]);
         }
-        host_prefill(ctx, prefix, n_floats);
-        itts::DecodeArgs a = decode_args(ctx);
-        a.mode = itts::kModeGenerate;
-        a.n_iter = max_tokens;
-        a.s0 = ctx->cached;
-        a.pos0 = 2;  // first generated code sits at mel position 2 (gpt_sampling.cpp:184-186)
-        a.opts = o;
-        launch_decode(ctx, a);
-        ck(cudaMemcpyAsync(ctx->h_codes, ctx->d_codes, size_t(max_tokens) * 4, cudaMemcpyDeviceToHost, ctx->stream),
-           "codes read");
-        check_status(ctx);
-        const itts::DecodeCtl& ctl = *ctx->h_ctl;
-        ctx->cached += ctl.info[3];
-        *n_codes = ctl.info[0];
-        *stopped = int(ctl.info[1]);
-        std::memcpy(codes, ctx->h_codes, size_t(ctl.info[0]) * 4);
+        for (size_t i = 0; i < batch; ++i)
+            generate_one(ctx, prefixes[i], n_floats[i], o[i], lp[i], max_tokens, codes + i * size_t(max_tokens),
+                         n_codes + i, stopped + i);
     });
 }
 

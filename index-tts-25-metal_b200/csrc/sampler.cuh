@@ -163,11 +163,15 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
         for (int k = 0; k < kPer; ++k) {
             const uint32_t key = ord_key(s[k]);
             const bool part = k < cnt && (key & mask) == prefix;
+            const uint32_t bin = (key >> shift) & 255u;
             const unsigned act = __ballot_sync(0xffffffffu, part);
-            if (part) {  // one shared-memory atomic per distinct bin of the warp
-                const uint32_t bin = (key >> shift) & 255u;
-                const unsigned peers = __match_any_sync(act, bin);
-                if (lane == __ffs(peers) - 1) atomicAdd(&sm.hist[bin], (uint32_t)__popc(peers));
+            if (act) {  // the lanes sharing the first participant's bin (most of them, as scores
+                        // cluster in a few high-order bins) add with one atomic; the rest singly
+                const int leader = __ffs(act) - 1;
+                const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
+                const unsigned same = __ballot_sync(0xffffffffu, part && bin == lb);
+                if (lane == leader) atomicAdd(&sm.hist[lb], (uint32_t)__popc(same));
+                if (part && bin != lb) atomicAdd(&sm.hist[bin], 1u);
             }
         }
         csync();
@@ -390,17 +394,49 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
         }
         if (tid == 0) {
             double total = 0.0;
-            for (uint32_t i = 0; i < n; ++i) total += pr ? pr[i] : exp(double(sc[i] - mx));
+            if (pr) {
+#pragma unroll 8
+                for (uint32_t i = 0; i < n; ++i) total += pr[i];
+            } else {
+                for (uint32_t i = 0; i < n; ++i) total += exp(double(sc[i] - mx));
+            }
             sm.err = total > 0.0 ? 0 : kStatusZeroMass;
             sm.f_total = total;
         }
         csync();
-        if (pr && !sm.err) {  // each survivor's share, in ascending order (same division as the reference)
+        if (pr && !sm.err) {
+            // each survivor's share in ascending order (the reference's division),
+            // then the cumulative mass by one thread in that order: the count of
+            // leading survivors whose mass stays <= 1 - p, removed in parallel
             const double total = sm.f_total;
             for (uint32_t j = tid; j < n; j += kThreads) sm.f_q[j] = pr[uint32_t(key[j])] / total;
             csync();
-        }
-        if (tid == 0 && !sm.err) {
+            if (tid == 0) {
+                const double low = 1.0 - double(o.top_p);
+                double cum = 0.0;
+                uint32_t nrem = 0;
+#pragma unroll 8
+                for (uint32_t j = 0; j < n; ++j) {
+                    cum += sm.f_q[j];
+                    if (!(cum <= low)) break;  // cumulative mass only grows: nothing later is removed
+                    nrem = j + 1;
+                }
+                sm.sel_rem = nrem;
+            }
+            csync();
+            for (uint32_t j = tid; j < sm.sel_rem; j += kThreads) {
+                const uint32_t t = idx[uint32_t(key[j])];
+                atomicOr(&sm.removed[t >> 5], 1u << (t & 31));
+            }
+            csync();
+            if (tid == 0) {
+                const uint32_t keep = (o.num_beams > 1 && n >= 2) ? 2u : 1u;
+                for (uint32_t i = 0; i < keep; ++i) {
+                    const uint32_t t = idx[uint32_t(key[n - 1 - i])];
+                    sm.removed[t >> 5] &= ~(1u << (t & 31));
+                }
+            }
+        } else if (tid == 0 && !sm.err) {
             const double total = sm.f_total;
             {
                 const double low = 1.0 - double(o.top_p);
@@ -440,8 +476,41 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
     }
     if (greedy) return block_argmax(s, base, cnt, sm);
 
-    // CDF sample in index order (thread 0, double precision).  The maximum is
-    // unchanged by top-p (the top score is always kept).
+    // CDF sample in index order (double precision).  The maximum is unchanged
+    // by top-p (the top score is always kept).  With the survivors' exp values
+    // cached, the mass of each survivor (0 when removed) is gathered in
+    // parallel and one thread folds it in index order as the reference does.
+    if (pr) {
+        csync();
+        for (uint32_t i = tid; i < n; i += kThreads) sm.f_q[i] = bit_get(sm.removed, idx[i]) ? 0.0 : pr[i];
+        csync();
+        if (tid == 0) {
+            double total = 0.0;
+#pragma unroll 8
+            for (uint32_t i = 0; i < n; ++i) total += sm.f_q[i];
+            if (!(total > 0.0)) {
+                set_status(status, kStatusZeroMass, 102, 0);
+                sm.result = 0xffffffffu;
+            } else {
+                const double target = uniform_at(o.rng, o.seed, draw) * total;
+                double cum = 0.0;
+                uint32_t last = 0, pick = 0xffffffffu;
+                for (uint32_t i = 0; i < n; ++i) {
+                    const double p = sm.f_q[i];
+                    if (p <= 0.0) continue;
+                    last = i;
+                    cum += p;
+                    if (target < cum) {
+                        pick = i;
+                        break;
+                    }
+                }
+                sm.result = idx[pick == 0xffffffffu ? last : pick];
+            }
+        }
+        csync();
+        return sm.result;
+    }
     if (tid == 0) {
         double total = 0.0;
         for (uint32_t i = 0; i < n; ++i)

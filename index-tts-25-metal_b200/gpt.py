@@ -72,6 +72,7 @@ SIGNATURES = {
     "itts_gpt_step": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P]),
     "itts_gpt_generate": (C.c_int, [_P, _P, C.c_size_t, C.POINTER(GenOpts), C.c_uint32, _P,
                                     C.POINTER(C.c_uint32), C.POINTER(C.c_int)]),
+    "itts_gpt_generate_batch": (C.c_int, [_P, C.c_size_t, _P, _P, _P, C.c_uint32, _P, _P, _P]),
     "itts_gpt_checkpoint": (C.c_int, [_P, C.POINTER(_P)]),
     "itts_gpt_restore": (C.c_int, [_P, _P]),
     "itts_gpt_state_free": (None, [_P]),
@@ -241,6 +242,24 @@ class GptDecoder:
         self._check(self._lib.itts_gpt_generate(self._h, _ptr(p), p.size, C.byref(opts), max_tokens, _ptr(codes),
                                                 C.byref(n), C.byref(st)))
         return GenerationResult(codes[:n.value].copy(), bool(st.value))
+
+    def generate_batch(self, prefixes, options, max_tokens: int = 1500) -> list:
+        """Independent requests (prefix i with options i) in one call; one
+        GenerationResult per request, as generate() would return it."""
+        ps = [_f32(p).ravel() for p in prefixes]
+        b = len(ps)
+        if len(options) != b:
+            raise ValueError("one GenOpts per prefix")
+        ptrs = (C.c_void_p * max(1, b))(*[p.ctypes.data for p in ps])
+        sizes = (C.c_size_t * max(1, b))(*[p.size for p in ps])
+        opts = (GenOpts * max(1, b))(*options)
+        codes = np.zeros((max(1, b), max(1, max_tokens)), np.uint32)
+        n = np.zeros(max(1, b), np.uint32)
+        st = np.zeros(max(1, b), np.int32)
+        self._check(self._lib.itts_gpt_generate_batch(self._h, b, C.cast(ptrs, C.c_void_p), C.cast(sizes, C.c_void_p),
+                                                      C.cast(opts, C.c_void_p), max_tokens, _ptr(codes), _ptr(n),
+                                                      _ptr(st)))
+        return [GenerationResult(codes[i, :n[i]].copy(), bool(st[i])) for i in range(b)]
 
     def checkpoint(self) -> GptState:
         s = C.c_void_p()

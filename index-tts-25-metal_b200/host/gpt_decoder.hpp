@@ -104,6 +104,32 @@ public:
         r.stopped = stopped != 0;
         return r;
     }
+    // Independent requests in one call (itts_gpt_generate_batch).
+    std::vector<GenerationResult> generate_batch(const std::vector<std::vector<float>>& prefixes,
+                                                 const std::vector<GenerationOptions>& options,
+                                                 uint32_t max_tokens = 1500) {
+        if (prefixes.size() != options.size()) throw std::invalid_argument("one options entry per prefix");
+        const size_t b = prefixes.size();
+        std::vector<const float*> ptrs(b);
+        std::vector<size_t> sizes(b);
+        std::vector<itts_gen_opts> o(b);
+        for (size_t i = 0; i < b; ++i) {
+            ptrs[i] = prefixes[i].data();
+            sizes[i] = prefixes[i].size();
+            o[i] = to_c(options[i]);
+        }
+        const size_t stride = max_tokens ? max_tokens : 1;
+        std::vector<uint32_t> codes(b * stride), n(b);
+        std::vector<int> stopped(b);
+        check(itts_gpt_generate_batch(ctx_, b, ptrs.data(), sizes.data(), o.data(), max_tokens, codes.data(), n.data(),
+                                      stopped.data()));
+        std::vector<GenerationResult> out(b);
+        for (size_t i = 0; i < b; ++i) {
+            out[i].codes.assign(codes.begin() + i * stride, codes.begin() + i * stride + n[i]);
+            out[i].stopped = stopped[i] != 0;
+        }
+        return out;
+    }
     GptState checkpoint() const {
         itts_gpt_state* s = nullptr;
         check(itts_gpt_checkpoint(ctx_, &s));

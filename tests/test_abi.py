@@ -127,6 +127,7 @@ def test_null_arguments_are_rejected(lib, gpt_mod):
     assert lib.itts_gpt_prefill(None, None, 0, None) == gpt_mod.ERR_INVALID_ARGUMENT
     assert lib.itts_gpt_cached_tokens(None) == 0
     assert lib.itts_gpt_sync(None) == gpt_mod.ERR_INVALID_ARGUMENT
+    assert lib.itts_gpt_generate_batch(None, 0, None, None, None, 0, None, None, None) == gpt_mod.ERR_INVALID_ARGUMENT
 
 
 def test_bundle_writer_round_trip(tmp_path):

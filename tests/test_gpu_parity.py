@@ -152,6 +152,27 @@ def test_generate_options_match_oracle(dec_shallow, port_shallow, gpt_mod, oracl
     assert r.stopped == st
 
 
+def test_generate_batch_matches_single_requests(dec_shallow, port_shallow, gpt_mod, oracle_mod):
+    """itts_gpt_generate_batch: each request's codes equal the oracle's for that
+    request alone; a bad request anywhere in the batch is rejected before any
+    runs."""
+    rng = np.random.default_rng(21)
+    prefixes = [rng.standard_normal((n, 1280)).astype(np.float32) for n in (7, 40, 120)]
+    kws = [dict(do_sample=False), dict(seed=5, rng=1), dict(do_sample=False, num_beams=2)]
+    res = dec_shallow.generate_batch(prefixes, [gpt_mod.gen_opts(**k) for k in kws], 24)
+    assert len(res) == 3
+    for p, k, r in zip(prefixes, kws, res):
+        e, st = port_shallow.generate(p, oracle_mod.make_opts(**k), 24)
+        np.testing.assert_array_equal(r.codes, e)
+        assert r.stopped == st
+    before = dec_shallow.cached_tokens()
+    with pytest.raises(ValueError):
+        dec_shallow.generate_batch(prefixes, [gpt_mod.gen_opts(), gpt_mod.gen_opts(temperature=0.0),
+                                              gpt_mod.gen_opts()], 24)
+    assert dec_shallow.cached_tokens() == before
+    assert dec_shallow.generate_batch([], [], 24) == []
+
+
 def test_stop_code_ends_generation(gpt_mod, oracle_mod, shallow_bundle):
     """A bundle whose mel_head favours the stop code: the loop stops and the
     stop code is not returned (gpt_sampling.cpp:181)."""
