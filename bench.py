@@ -226,7 +226,8 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         path = bundle_path()
-    dec = gpt.GptDecoder(path, device=local)
+    wb = args.weights == "bf16"
+    dec = gpt.GptDecoder(path, device=local, weight_dtype=1 if wb else 0)
     info = dec.info()
     prefix = make_prefix(dec.prepare, 1002 + rank)
     rows = prefix.shape[0]
@@ -310,7 +311,7 @@ def run_ours(args):
     # small captured launch, applied to this launch's algorithmic bytes
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tpath):
+    if os.path.exists(tpath) and not wb:  # the captured ratio is the fp32 kernel's
         with open(tpath) as f:
             tj = json.load(f)
         if tj.get("capture_dram_bytes") and tj.get("capture_algorithmic_bytes"):
@@ -330,6 +331,7 @@ def run_ours(args):
             "config": {"workload": "configs[1]: sampled decode (T 0.8, top-k 30, top-p 0.8, rp 10, Philox "
                                    f"seed 1234), prefix 32 latents + 200 text tokens, {n_codes} codes, batch 1",
                        "model": "UnifiedVoice GPT 24L d1280 H20 FFN5120 fp32 random-init (seed 42)",
+                       "weights": "bf16 matrices (fp32 LN, bias, KV, accumulation)" if wb else "fp32",
                        "global_batch": world, "prefix_rows": rows, "codes_per_request": n_codes,
                        "parallelism": f"replicas x{world} (one request per GPU, no collective)",
                        "l2": "inputs larger than L2: each forward step streams 1.93 GB of weights (L2 126 MB)",
@@ -362,6 +364,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=48)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights", choices=["f32", "bf16"], default="f32",
+                    help="weight storage of the decoder (the headline is f32; bf16 is the optional weight path)")
     ap.add_argument("--codes", type=int, default=N_CODES,
                     help="codes per request (1024 is the benchmark; smaller values are for profiler captures)")
     args = ap.parse_args()

@@ -201,10 +201,15 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
     // device layout: every tensor 256-byte aligned in one allocation
     std::vector<std::pair<const itts::TensorInfo*, size_t>> plan;
     size_t total = 0;
+    // the streamed matrices (Conv1D blocks and mel_head) are bf16 in a bf16 context
+    const bool wb = c->dtype == ITTS_WEIGHTS_BF16;
+    auto is_conv = [](const itts::TensorInfo& t) { return t.name.rfind("gpt.gpt.h.", 0) == 0 && t.shape.size() == 2; };
+    auto is_matrix = [&](const itts::TensorInfo& t) { return is_conv(t) || t.name == "gpt.mel_head.weight"; };
+    auto dev_bytes = [&](const itts::TensorInfo& t) { return wb && is_matrix(t) ? t.nbytes / 2 : t.nbytes; };
     auto add = [&](const std::string& n) {
         const auto* t = &b.info(n);
         plan.emplace_back(t, total);
-        total += align256(t->nbytes);
+        total += align256(dev_bytes(*t));
         return plan.size() - 1;
     };
     std::vector<size_t> idx;
@@ -226,19 +231,24 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
     c->d_weights = dev_alloc<char>(total, "weight allocation");
     c->weight_bytes = total;
 
-    // upload; Conv1D matrices go through a staging buffer and a transpose
-    float* stage = dev_alloc<float>(size_t(5120) * 1280, "transpose staging");
+    // upload; Conv1D matrices go through a staging buffer and a transpose,
+    // bf16 matrices are rounded to nearest even on the device
+    float* stage = dev_alloc<float>(size_t(wb ? 8194 : 5120) * 1280, "transpose staging");
     try {
         for (const auto& pe : plan) {
             const itts::TensorInfo& t = *pe.first;
             char* dst = c->d_weights + pe.second;
-            const bool is_conv = t.name.rfind("gpt.gpt.h.", 0) == 0 && t.shape.size() == 2;
-            if (is_conv) {
+            if (is_conv(t)) {
                 ck(cudaMemcpy(stage, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
-                ck(itts::launch_transpose(stage, reinterpret_cast<float*>(dst), int(t.shape[0]), int(t.shape[1]),
-                                          nullptr),
+                ck(wb ? itts::launch_transpose_bf16(stage, dst, int(t.shape[0]), int(t.shape[1]), nullptr)
+                      : itts::launch_transpose(stage, reinterpret_cast<float*>(dst), int(t.shape[0]),
+                                               int(t.shape[1]), nullptr),
                    "transpose launch");
                 ck(cudaDeviceSynchronize(), "transpose");
+            } else if (wb && is_matrix(t)) {
+                ck(cudaMemcpy(stage, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+                ck(itts::launch_to_bf16(stage, dst, t.nbytes / 4, nullptr), "bf16 conversion launch");
+                ck(cudaDeviceSynchronize(), "bf16 conversion");
             } else {
                 ck(cudaMemcpy(dst, b.data(t), t.nbytes, cudaMemcpyHostToDevice), "weight upload");
             }
@@ -293,8 +303,11 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
     }
     c->hw.head_pack1 = put(packs + size_t(layers) * 4 * kRow, c->hw.lnf_g, c->hw.lnf_b);
     c->hw.head_pack2 = put(packs + (size_t(layers) * 4 + 2) * kRow, c->hw.fn_g, c->hw.fn_b);
-    const uint64_t per_layer_floats = 19660800ull + 11520ull + 5120ull;
-    c->stream_bytes = 4ull * (per_layer_floats * layers + 10488320ull + 8194ull + 5120ull + 2560ull);
+    // algorithmic bytes streamed per decode step: matrices, biases, LayerNorms,
+    // mel_head and its bias, the final LayerNorms, two embedding rows
+    const uint64_t mat_elems = 19660800ull * layers + 10488320ull;
+    const uint64_t vec_floats = (11520ull + 5120ull) * layers + 8194ull + 5120ull + 2560ull;
+    c->stream_bytes = (wb ? 2ull : 4ull) * mat_elems + 4ull * vec_floats;
 }
 
 void alloc_buffers(itts_gpt_ctx* c) {
@@ -394,21 +407,29 @@ void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     // epochs restart at 1 in every launch: clear the tagged hand-off words
     ck(cudaMemsetAsync(c->db.qkv, 0, c->tagged_bytes, c->stream), "hand-off reset");
     if (c->mode == 0) {
-        ck(itts::launch_decode_persistent(a, c->sm_count, c->stream), "persistent decode launch");
+        ck(c->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_decode_persistent(a, c->sm_count, c->stream)
+                                         : itts::wf32::launch_decode_persistent(a, c->sm_count, c->stream),
+           "persistent decode launch");
         ++c->launches;
     } else {
-        ck(itts::launch_decode_layered(a, int(c->layers), c->sm_count, c->stream, &c->launches), "layered decode launch");
+        ck(c->dtype == ITTS_WEIGHTS_BF16
+               ? itts::wbf16::launch_decode_layered(a, int(c->layers), c->sm_count, c->stream, &c->launches)
+               : itts::wf32::launch_decode_layered(a, int(c->layers), c->sm_count, c->stream, &c->launches),
+           "layered decode launch");
     }
 }
 
 // prefix already in d_hidden
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
-    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x, c->d_qkv, c->d_att, c->d_r, c->d_ff, c->d_kv, int(rows)};
+    itts::PrefillArgs p{&c->hw,  c->d_hidden, c->d_x,     c->d_qkv, c->d_att,
+                        c->d_r,  c->d_ff,     c->d_kv,    int(rows), c->dtype == ITTS_WEIGHTS_BF16};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     reset_ctl(c);
     itts::DecodeArgs a = decode_args(c);
     a.head_src = c->d_hidden + size_t(rows - 1) * kW;
-    ck(itts::launch_head(a, c->sm_count, c->stream), "head launch");
+    ck(c->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_head(a, c->sm_count, c->stream)
+                                     : itts::wf32::launch_head(a, c->sm_count, c->stream),
+       "head launch");
     ++c->launches;
 }
 
@@ -709,8 +730,8 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
     c->dtype = weight_dtype;
     const int rc = guard(c.get(), [&] {
         if (!bundle_dir) invalid("bundle_dir is null");
-        if (weight_dtype != ITTS_WEIGHTS_F32)
-            invalid("weight_dtype: only ITTS_WEIGHTS_F32 is available in this build");
+        if (weight_dtype != ITTS_WEIGHTS_F32 && weight_dtype != ITTS_WEIGHTS_BF16)
+            invalid("weight_dtype must be ITTS_WEIGHTS_F32 or ITTS_WEIGHTS_BF16");
         itts::Mit2Bundle bundle(bundle_dir);
         validate_bundle(c.get(), bundle);
         int n = 0;
@@ -725,7 +746,10 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
         if ((8194 + c->sm_count - 1) / c->sm_count > 64) fail(ITTS_ERR_RUNTIME, "device has too few SMs");
         if (!prop.cooperativeLaunch) fail(ITTS_ERR_RUNTIME, "device lacks cooperative launch");
         int per_sm = 0;
-        ck(itts::decode_configure(&per_sm), "decode kernel configuration");
+        ck(itts::sampler_configure(), "sampler kernel configuration");
+        ck(weight_dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::decode_configure(&per_sm)
+                                             : itts::wf32::decode_configure(&per_sm),
+           "decode kernel configuration");
         if (per_sm < 1) fail(ITTS_ERR_RUNTIME, "persistent decode kernel does not fit on an SM");
         ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream creation");
         upload_weights(c.get(), bundle);

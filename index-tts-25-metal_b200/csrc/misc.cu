@@ -1,5 +1,7 @@
 // Load-time and conditioning kernels: the Conv1D weight transpose and
 // GptDecoder::prepare on the device.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "model.hpp"
 
@@ -7,7 +9,11 @@ namespace itts {
 
 // out[c, r] = in[r, c] for in [rows_in, cols_in] (HF Conv1D [in, out] ->
 // row-major [out, in], the transpose gpt.cpp:24-33 caches on the CPU).
-__global__ void k_transpose(const float* __restrict__ in, float* __restrict__ out, int rows_in, int cols_in) {
+__device__ __forceinline__ void store_w(float* p, float v) { *p = v; }
+__device__ __forceinline__ void store_w(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <class T>
+__global__ void k_transpose(const float* __restrict__ in, T* __restrict__ out, int rows_in, int cols_in) {
     __shared__ float tile[32][33];
     const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -17,13 +23,29 @@ __global__ void k_transpose(const float* __restrict__ in, float* __restrict__ ou
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int c = c0 + i, r = r0 + threadIdx.x;
-        if (r < rows_in && c < cols_in) out[(size_t)c * rows_in + r] = tile[threadIdx.x][i];
+        if (r < rows_in && c < cols_in) store_w(out + (size_t)c * rows_in + r, tile[threadIdx.x][i]);
     }
 }
 
 cudaError_t launch_transpose(const float* in, float* out, int rows_in, int cols_in, cudaStream_t s) {
     dim3 grid((cols_in + 31) / 32, (rows_in + 31) / 32);
-    k_transpose<<<grid, dim3(32, 8), 0, s>>>(in, out, rows_in, cols_in);
+    k_transpose<float><<<grid, dim3(32, 8), 0, s>>>(in, out, rows_in, cols_in);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_bf16(const float* in, void* out, int rows_in, int cols_in, cudaStream_t s) {
+    dim3 grid((cols_in + 31) / 32, (rows_in + 31) / 32);
+    k_transpose<__nv_bfloat16><<<grid, dim3(32, 8), 0, s>>>(in, static_cast<__nv_bfloat16*>(out), rows_in, cols_in);
+    return cudaGetLastError();
+}
+
+__global__ void k_to_bf16(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __float2bfloat16_rn(in[i]);
+}
+
+cudaError_t launch_to_bf16(const float* in, void* out, size_t n, cudaStream_t s) {
+    k_to_bf16<<<1184, 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n);
     return cudaGetLastError();
 }
 

@@ -106,13 +106,27 @@ struct DecodeArgs {
     const float* head_src;  // prefill: last hidden row fed to the head phase
 };
 
-// ---- host-side launchers (decode.cu, prefill.cu, misc.cu) -----------------
-size_t decode_smem_bytes();
+// ---- host-side launchers ----------------------------------------------------
+// decode_body.cuh, once per weight type: wf32 (decode.cu), wbf16 (decode_bf16.cu)
+#define ITTS_DECLARE_DECODE_LAUNCHERS(NS)                                                                      \
+    namespace NS {                                                                                             \
+    size_t decode_smem_bytes();                                                                                \
+    cudaError_t decode_configure(int* blocks_per_sm);                                                          \
+    cudaError_t launch_decode_persistent(const DecodeArgs& a, int ncta, cudaStream_t s);                       \
+    cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cudaStream_t s,               \
+                                      uint64_t* launches);                                                     \
+    cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s);                                    \
+    }
+ITTS_DECLARE_DECODE_LAUNCHERS(wf32)
+ITTS_DECLARE_DECODE_LAUNCHERS(wbf16)
+#undef ITTS_DECLARE_DECODE_LAUNCHERS
+
+// sampler_kernels.cu
 size_t sampler_big_bytes();
-cudaError_t decode_configure(int* blocks_per_sm);
-cudaError_t launch_decode_persistent(const DecodeArgs& a, int ncta, cudaStream_t s);
-cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cudaStream_t s, uint64_t* launches);
-cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s);
+size_t sampler_dyn_smem_bytes();
+cudaError_t sampler_configure();
+cudaError_t launch_layer_sample(const DecodeArgs& a, uint32_t i, cudaStream_t s);
+cudaError_t launch_layer_finish(const DecodeArgs& a, cudaStream_t s);
 cudaError_t launch_processors(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
                               float* out, int* status, cudaStream_t s);
 
@@ -126,10 +140,13 @@ struct PrefillArgs {
     float* ff;         // [T, 5120]
     float* kv;
     int T;
+    bool wbf16;  // matrices stored bf16
 };
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
 
 cudaError_t launch_transpose(const float* in, float* out, int rows_in, int cols_in, cudaStream_t s);
+cudaError_t launch_transpose_bf16(const float* in, void* out, int rows_in, int cols_in, cudaStream_t s);
+cudaError_t launch_to_bf16(const float* in, void* out, size_t n, cudaStream_t s);
 struct PrepareArgs {
     const float *spk_w, *spk_b, *text_emb, *text_pos, *lang_emb, *mel_emb, *mel_pos;
     const float *speaker, *emotion;

@@ -42,8 +42,10 @@ __global__ void __launch_bounds__(256) k_ln_rows(const float* __restrict__ x, co
 
 enum GemmEpi : int { kEpiBias = 0, kEpiGelu = 1, kEpiResid = 2 };
 
-template <int EPI>
-__global__ void __launch_bounds__(256) k_gemm_nt(const float* __restrict__ A, const float* __restrict__ W,
+// W is fp32, or bf16 when WB (widened to fp32 on load: bf16 is the high half
+// of an fp32 word).
+template <int EPI, bool WB>
+__global__ void __launch_bounds__(256) k_gemm_nt(const float* __restrict__ A, const void* __restrict__ Wv,
                                                  const float* __restrict__ bias, const float* __restrict__ R,
                                                  float* __restrict__ C, int M, int N, int K) {
     constexpr int BM = 64, BN = 64, BK = 16;
@@ -56,8 +58,16 @@ __global__ void __launch_bounds__(256) k_gemm_nt(const float* __restrict__ A, co
     auto gload = [&](int k0) {
         ra = (m0 + lr < M) ? *reinterpret_cast<const float4*>(A + (size_t)(m0 + lr) * K + k0 + lk)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        rw = (n0 + lr < N) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(n0 + lr) * K + k0 + lk))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n0 + lr >= N) {
+            rw = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if (WB) {
+            const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(Wv) +
+                                                                 (size_t)(n0 + lr) * K + k0 + lk));
+            rw = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                             __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+        } else {
+            rw = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(Wv) + (size_t)(n0 + lr) * K + k0 + lk));
+        }
     };
     auto sstore = [&](int buf) {
         As[buf][lk + 0][lr] = ra.x;
@@ -193,10 +203,13 @@ __global__ void __launch_bounds__(512) k_causal_attn(const float* __restrict__ q
 }
 
 template <int EPI>
-static void gemm(const float* A, const float* W, const float* bias, const float* R, float* C, int M, int N, int K,
-                 cudaStream_t s) {
+static void gemm(const float* A, const float* W, bool wb, const float* bias, const float* R, float* C, int M, int N,
+                 int K, cudaStream_t s) {
     dim3 grid((N + 63) / 64, (M + 63) / 64);
-    k_gemm_nt<EPI><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
+    if (wb)
+        k_gemm_nt<EPI, true><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
+    else
+        k_gemm_nt<EPI, false><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
 }
 
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
@@ -204,14 +217,14 @@ cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t
     for (int l = 0; l < p.hw->layers; ++l) {
         const LayerW& L = p.hw->layer[l];
         k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, p.x);
-        gemm<kEpiBias>(p.x, L.w_qkv, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, s);
+        gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, s);
         k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
             p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
         k_causal_attn<<<dim3(kHeads, (T + 15) / 16), 512, 0, s>>>(p.qkv, p.att, T);
-        gemm<kEpiResid>(p.att, L.w_o, L.b_o, p.hidden, p.r, T, kWidth, kWidth, s);
+        gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, s);
         k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x);
-        gemm<kEpiGelu>(p.x, L.w_fc, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, s);
-        gemm<kEpiResid>(p.ff, L.w_mp, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, s);
+        gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, s);
+        gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, s);
         *launches += 8;
     }
     return cudaGetLastError();

@@ -102,15 +102,32 @@ def bundle_complete(path: str) -> bool:
         os.path.exists(os.path.join(path, ".complete"))
 
 
+def is_streamed_matrix(name: str) -> bool:
+    """The matrices a bf16-weight decoder stores as bf16."""
+    return name == "gpt.mel_head.weight" or (name.startswith("gpt.gpt.h.") and name.endswith(
+        (".attn.c_attn.weight", ".attn.c_proj.weight", ".mlp.c_fc.weight", ".mlp.c_proj.weight")))
+
+
+def round_to_bf16(v: np.ndarray) -> np.ndarray:
+    """fp32 values rounded to the nearest bf16 (ties to even), as fp32; finite inputs."""
+    u = np.ascontiguousarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(np.shape(v))
+
+
 def write_synthetic_gpt_bundle(path: str, *, seed: int = 42, layers: int = 24,
                                mask_stop: bool = False, std: float = 0.02,
                                mel_pos_rows: int = MEL_POS_ROWS,
-                               alignment: int = 256, reuse: bool = True) -> str:
+                               alignment: int = 256, reuse: bool = True, bf16_exact: bool = False) -> str:
     """Write a random-init GPT bundle to ``path`` (a directory) and return the
     SHA-256 of ``weights.bin``.  An existing complete bundle written with the same
-    arguments is reused (its recorded hash is returned)."""
+    arguments is reused (its recorded hash is returned).  ``bf16_exact`` rounds
+    the streamed matrices (c_attn, attn.c_proj, c_fc, mlp.c_proj, mel_head) to
+    bf16-representable values, so a bf16-weight decoder stores them exactly."""
     args = dict(seed=seed, layers=layers, mask_stop=bool(mask_stop), std=std,
                 mel_pos_rows=mel_pos_rows, alignment=alignment)
+    if bf16_exact:
+        args["bf16_exact"] = True
     os.makedirs(path, exist_ok=True)
     marker = os.path.join(path, ".complete")
     if reuse and bundle_complete(path):
@@ -131,6 +148,8 @@ def write_synthetic_gpt_bundle(path: str, *, seed: int = 42, layers: int = 24,
         h.update(header)
         for idx, (name, shape, kind) in enumerate(specs):
             v = _tensor_values(seed, idx, shape, kind, std)
+            if bf16_exact and is_streamed_matrix(name):
+                v = round_to_bf16(v)
             if mask_stop and name == "gpt.mel_head.bias":
                 v[STOP_CODE] = np.float32(-1e30)
             raw = v.tobytes()

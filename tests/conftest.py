@@ -27,9 +27,10 @@ def golden(name: str):
     return np.load(os.path.join(GOLDEN, name))
 
 
-def synthetic_bundle(seed: int, layers: int, mask_stop: bool, expect_sha: str | None = None) -> str:
-    path = os.path.join(CACHE, f"gpt_s{seed}_l{layers}_m{int(mask_stop)}")
-    sha = mit2.write_synthetic_gpt_bundle(path, seed=seed, layers=layers, mask_stop=mask_stop)
+def synthetic_bundle(seed: int, layers: int, mask_stop: bool, expect_sha: str | None = None,
+                     bf16_exact: bool = False) -> str:
+    path = os.path.join(CACHE, f"gpt_s{seed}_l{layers}_m{int(mask_stop)}" + ("_bf16x" if bf16_exact else ""))
+    sha = mit2.write_synthetic_gpt_bundle(path, seed=seed, layers=layers, mask_stop=mask_stop, bf16_exact=bf16_exact)
     if expect_sha is not None and sha != expect_sha:
         raise RuntimeError(f"synthetic bundle {path} does not reproduce the fixture's weights "
                            f"(sha {sha} != {expect_sha})")
@@ -51,6 +52,11 @@ def long_bundle():
 @pytest.fixture(scope="session")
 def shallow_bundle():
     return synthetic_bundle(7, 2, False)
+
+
+@pytest.fixture(scope="session")
+def shallow_bf16_bundle():
+    return synthetic_bundle(7, 2, False, bf16_exact=True)
 
 
 @pytest.fixture(scope="session")
