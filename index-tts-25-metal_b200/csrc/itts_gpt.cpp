@@ -421,8 +421,8 @@ void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
 
 // prefix already in d_hidden
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
-    itts::PrefillArgs p{&c->hw,  c->d_hidden, c->d_x,     c->d_qkv, c->d_att,
-                        c->d_r,  c->d_ff,     c->d_kv,    int(rows), c->dtype == ITTS_WEIGHTS_BF16};
+    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x,    c->d_qkv,  c->d_att, c->d_r, c->d_ff,
+                        c->d_kv, int(rows),   c->dtype == ITTS_WEIGHTS_BF16, c->db.ctl->status};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     reset_ctl(c);
     itts::DecodeArgs a = decode_args(c);

@@ -140,7 +140,8 @@ struct PrefillArgs {
     float* ff;         // [T, 5120]
     float* kv;
     int T;
-    bool wbf16;  // matrices stored bf16
+    bool wbf16;   // matrices stored bf16
+    int* status;  // device status word (bounded waits of the tensor-core GEMM)
 };
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
 

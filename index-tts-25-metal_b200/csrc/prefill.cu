@@ -202,9 +202,22 @@ __global__ void __launch_bounds__(512) k_causal_attn(const float* __restrict__ q
     }
 }
 
+bool gemm_tc_supported(int N, int K);
+cudaError_t launch_gemm_tc(int epi, bool wbf16, const float* A, const void* W, const float* bias, const float* R,
+                           float* C, int M, int N, int K, int* status, cudaStream_t s);
+
+// The tensor-core GEMM (gemm_tc.cu, three TF32 products) serves the bf16-
+// weight path.  fp32 weights keep the SIMT tiles above: the tensor core's fp32
+// accumulation, even drained every 256 K, leaves prefill logits about 3x
+// further from the reference (8e-6 vs 3e-6 max_abs on the 24-layer model),
+// enough to change a 1024-code sampled run that the fp32 path reproduces.
 template <int EPI>
 static void gemm(const float* A, const float* W, bool wb, const float* bias, const float* R, float* C, int M, int N,
-                 int K, cudaStream_t s) {
+                 int K, int* status, cudaStream_t s) {
+    if (wb && gemm_tc_supported(N, K)) {
+        launch_gemm_tc(EPI, wb, A, W, bias, R, C, M, N, K, status, s);
+        return;
+    }
     dim3 grid((N + 63) / 64, (M + 63) / 64);
     if (wb)
         k_gemm_nt<EPI, true><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
@@ -217,14 +230,14 @@ cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t
     for (int l = 0; l < p.hw->layers; ++l) {
         const LayerW& L = p.hw->layer[l];
         k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, p.x);
-        gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, s);
+        gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, p.status, s);
         k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
             p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
         k_causal_attn<<<dim3(kHeads, (T + 15) / 16), 512, 0, s>>>(p.qkv, p.att, T);
-        gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, s);
+        gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, p.status, s);
         k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x);
-        gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, s);
-        gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, s);
+        gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, p.status, s);
+        gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, p.status, s);
         *launches += 8;
     }
     return cudaGetLastError();
