@@ -60,6 +60,12 @@ constexpr int kRowBytes = kWidth * kWBytes;            // one 1280-wide matrix r
 constexpr int kPackBytes = 2 * kWidth * 4;             // a LayerNorm's fp32 [gamma, beta]
 constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 40 KB
 constexpr int kSlots = 5;
+// Bulk copies a CTA keeps in flight.  One suffices for the weight stream
+// (148 x 40 KB outstanding covers the HBM latency at the rate the layers
+// consume), and more only lengthens the memory queues that every hand-off
+// load and store also waits in: the ring refills after a phase in a paced
+// trickle instead of a burst of five copies from every CTA at once.
+constexpr int kInFlight = 1;
 // Consumer geometry: warp w works on row w / kWarpsPerRow of a slot and on
 // column block w % kWarpsPerRow (kColsPerWarp wide); lane l reads 8 bytes per
 // load (2 fp32 or 4 bf16 weights) and holds the matching kVec float2 of the
@@ -129,6 +135,7 @@ struct DecodeSmem {
     SamplerSmem sa;
     ModelW w;  // the weight pointer table, read at every slot and phase start
 };
+static_assert(kInFlight >= 1 && kInFlight < kSlots, "paced copies must stay inside the ring");
 static_assert(sizeof(DecodeSmem) <= 227 * 1024, "decode kernel shared memory above the sm_100 per-CTA limit");
 
 // All threads: copy the weight pointer table into shared memory.
@@ -290,7 +297,8 @@ __device__ bool wait_empty(Ring& R, int s, uint32_t parity, int* status, uint32_
 
 // Producer warp (lane 0): issues segments [k0, k1) of each of n_steps forward
 // steps into the ring, one bulk copy per slot, waiting for a slot's previous
-// use to be handed back before reusing it.
+// use to be handed back before reusing it and for the copy kInFlight slots
+// back to have landed before issuing the next.
 __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Rows& rows, int k0, int k1, int n_steps) {
     int* status = a.b.ctl->status;
     uint32_t j = 0, parity = 0;
@@ -305,6 +313,10 @@ __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Ro
             seg_of(w, rows, k, p, bytes);
             for (uint32_t off = 0; off < bytes; off += kSlotBytes) {
                 const uint32_t n = min(bytes - off, (uint32_t)kSlotBytes);
+                if (j >= kInFlight) {  // that slot is still in the ring (kInFlight < kSlots)
+                    const uint32_t jp = j - kInFlight;
+                    if (!mbar_wait_bounded(&R.full[jp % kSlots], (jp / kSlots) & 1u, status, 901)) goto done;
+                }
                 if (j >= kSlots &&
                     !wait_empty(R, s, parity ^ 1u, status, j, w, rows, k0, k1, n_steps, pf, issued))
                     goto done;
