@@ -50,22 +50,22 @@ namespace ITTS_WNS {
 // ------------------------------------------------------------ weight ring
 #if ITTS_WBF16
 using wtype = __nv_bfloat16;  // element of the streamed weight matrices
-constexpr int kRowsPerSlot = 16;  // rows of 1280 per slot
+constexpr int kRowsPerSlot = 8;  // rows of 1280 per slot
 #else
 using wtype = float;
-constexpr int kRowsPerSlot = 8;
+constexpr int kRowsPerSlot = 4;
 #endif
 constexpr int kWBytes = int(sizeof(wtype));
 constexpr int kRowBytes = kWidth * kWBytes;            // one 1280-wide matrix row
 constexpr int kPackBytes = 2 * kWidth * 4;             // a LayerNorm's fp32 [gamma, beta]
-constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 40 KB
-constexpr int kSlots = 5;
-// Bulk copies a CTA keeps in flight.  One suffices for the weight stream
-// (148 x 40 KB outstanding covers the HBM latency at the rate the layers
-// consume), and more only lengthens the memory queues that every hand-off
-// load and store also waits in: the ring refills after a phase in a paced
-// trickle instead of a burst of five copies from every CTA at once.
-constexpr int kInFlight = 1;
+constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 20 KB
+constexpr int kSlots = 10;
+// Bulk copies a CTA keeps in flight.  Two 20 KB copies (148 x 40 KB
+// outstanding) cover the HBM latency at the rate the layers consume; more only
+// lengthens the memory queues that every hand-off load and store also waits
+// in: the ring refills after a phase in a paced trickle instead of a burst of
+// copies from every CTA at once.
+constexpr int kInFlight = 2;
 // Consumer geometry: warp w works on row w / kWarpsPerRow of a slot and on
 // column block w % kWarpsPerRow (kColsPerWarp wide); lane l reads 8 bytes per
 // load (2 fp32 or 4 bf16 weights) and holds the matching kVec float2 of the
