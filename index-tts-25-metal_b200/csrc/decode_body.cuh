@@ -16,12 +16,13 @@
 // only grid barrier of a step follows the head.
 //
 // Weight streaming: every CTA owns a contiguous block of rows per matrix.  Its
-// rows (and the LayerNorm packs) are fetched into a 5-slot x 40 KB shared-
-// memory ring with cp.async.bulk (1-D TMA, completion on a "full" mbarrier,
-// L2 evict-first; no multicast) by a dedicated producer warp that walks the
-// CTA's segment schedule; the 16 consumer warps hand a slot back on its
-// "empty" mbarrier, and while the ring is full the producer prefetches further
-// ahead into L2.  The stream therefore runs through the hand-off waits, the
+// rows are fetched into a 10-slot x 20 KB shared-memory ring with
+// cp.async.bulk (1-D TMA, completion on a "full" mbarrier, L2 evict-first; no
+// multicast) by a dedicated producer warp that walks the CTA's segment
+// schedule, two copies in flight at a time; the 16 consumer warps hand a slot
+// back on its "empty" mbarrier, and while the ring is full the producer
+// prefetches further ahead into L2.  LayerNorm vectors are loaded into
+// registers (each lane's columns) when a phase starts waiting for its input.  The stream therefore runs through the hand-off waits, the
 // attention phase and the sampler, which are the latency-bound parts of the
 // step.
 //
@@ -57,7 +58,6 @@ constexpr int kRowsPerSlot = 4;
 #endif
 constexpr int kWBytes = int(sizeof(wtype));
 constexpr int kRowBytes = kWidth * kWBytes;            // one 1280-wide matrix row
-constexpr int kPackBytes = 2 * kWidth * 4;             // a LayerNorm's fp32 [gamma, beta]
 constexpr int kSlotBytes = kRowsPerSlot * kRowBytes;  // 20 KB
 constexpr int kSlots = 10;
 // Bulk copies a CTA keeps in flight.  Two 20 KB copies (148 x 40 KB
@@ -75,7 +75,6 @@ constexpr int kWarpsPerRow = kWarps / kRowsPerSlot;
 constexpr int kColsPerWarp = kWidth / kWarpsPerRow;
 constexpr int kVec = kColsPerWarp / 64;
 constexpr int kLongPerSlot = kSlotBytes / (kFfn * kWBytes);
-static_assert(kPackBytes <= kSlotBytes, "a LayerNorm pack fits one slot");
 constexpr int kWarpsPerLong = kWarps / kLongPerSlot;
 static_assert(kWarpsPerRow * kRowsPerSlot == kWarps && kColsPerWarp % 64 == 0, "slot geometry");
 static_assert(kWarpsPerLong * kColsPerWarp == kFfn, "5120-wide rows use the same per-warp width");
@@ -206,34 +205,32 @@ __device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, int*
 }
 
 // The weight schedule of one CTA, as segments of contiguous bytes; segment k
-// of a forward step (6 per layer, then 3 for the head):
-//   6l+0 ln_1 pack           6l+1 its c_attn rows     6l+2 its attn.c_proj rows
-//   6l+3 ln_2 pack           6l+4 its c_fc rows       6l+5 its mlp.c_proj rows (5120 wide)
-//   6L+0 ln_f pack           6L+1 final_norm pack     6L+2 its mel_head rows
-// Segments are cut into 20 KB slots (4 rows of 1280, or one row of 5120).
+// of a forward step (4 per layer, then 1 for the head):
+//   4l+0 its c_attn rows     4l+1 its attn.c_proj rows
+//   4l+2 its c_fc rows       4l+3 its mlp.c_proj rows (5120 wide)
+//   4L   its mel_head rows
+// Segments are cut into kSlotBytes slots (kRowsPerSlot rows of 1280, or
+// kRowsPerSlot / 4 rows of 5120).
+constexpr int kSegsPerLayer = 4;
 __device__ __forceinline__ void seg_of(const ModelW& w, const Rows& r, int k, const char*& p, uint32_t& bytes) {
     auto rows_of = [](const float* m, int r0, int r1, int width) {  // matrix rows [r0, r1) of `width` weights
         return reinterpret_cast<const char*>(m) + (size_t)r0 * width * kWBytes;
     };
-    if (k < 6 * w.layers) {
-        const LayerW& lw = w.layer[k / 6];
-        switch (k % 6) {
-            case 0: p = reinterpret_cast<const char*>(lw.ln1_pack); bytes = kPackBytes; break;
-            case 1: p = rows_of(lw.w_qkv, r.q0, r.q1, kWidth); bytes = uint32_t(r.q1 - r.q0) * kRowBytes; break;
-            case 2: p = rows_of(lw.w_o, r.o0, r.o1, kWidth); bytes = uint32_t(r.o1 - r.o0) * kRowBytes; break;
-            case 3: p = reinterpret_cast<const char*>(lw.ln2_pack); bytes = kPackBytes; break;
-            case 4: p = rows_of(lw.w_fc, r.f0, r.f1, kWidth); bytes = uint32_t(r.f1 - r.f0) * kRowBytes; break;
+    if (k < kSegsPerLayer * w.layers) {
+        const LayerW& lw = w.layer[k / kSegsPerLayer];
+        switch (k % kSegsPerLayer) {
+            case 0: p = rows_of(lw.w_qkv, r.q0, r.q1, kWidth); bytes = uint32_t(r.q1 - r.q0) * kRowBytes; break;
+            case 1: p = rows_of(lw.w_o, r.o0, r.o1, kWidth); bytes = uint32_t(r.o1 - r.o0) * kRowBytes; break;
+            case 2: p = rows_of(lw.w_fc, r.f0, r.f1, kWidth); bytes = uint32_t(r.f1 - r.f0) * kRowBytes; break;
             default: p = rows_of(lw.w_mp, r.o0, r.o1, kFfn); bytes = uint32_t(r.o1 - r.o0) * kFfn * kWBytes; break;
         }
     } else {
-        const int h = k - 6 * w.layers;
-        if (h == 0) { p = reinterpret_cast<const char*>(w.head_pack1); bytes = kPackBytes; }
-        else if (h == 1) { p = reinterpret_cast<const char*>(w.head_pack2); bytes = kPackBytes; }
-        else { p = rows_of(w.w_head, r.h0, r.h1, kWidth); bytes = uint32_t(r.h1 - r.h0) * kRowBytes; }
+        p = rows_of(w.w_head, r.h0, r.h1, kWidth);
+        bytes = uint32_t(r.h1 - r.h0) * kRowBytes;
     }
 }
 
-__device__ __forceinline__ int segs_per_step(const ModelW& w) { return 6 * w.layers + 3; }
+__device__ __forceinline__ int segs_per_step(const ModelW& w) { return kSegsPerLayer * w.layers + 1; }
 
 // Schedule position of the L2 prefetch that runs ahead of the ring.
 struct PfCursor {
@@ -419,7 +416,7 @@ __device__ __forceinline__ void chan_merge(float& m, float& M2, float mb, float 
 // per-thread mean and centred sum of squares, merged pairwise across lanes
 // and then across the group's warps (one group barrier), the same operations
 // in the same order in every group.
-__device__ void layernorm2(float2 (&x)[kVec], const float* g, const float* b, float (*wstat)[2]) {
+__device__ void layernorm2(float2 (&x)[kVec], const float2 (&g)[kVec], const float2 (&b)[kVec], float (*wstat)[2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float m = 0.f;
 #pragma unroll
@@ -471,20 +468,22 @@ __device__ void layernorm2(float2 (&x)[kVec], const float* g, const float* b, fl
     const float inv = 1.0f / sqrtf(var + kLnEps);
 #pragma unroll
     for (int j = 0; j < kVec; ++j) {
-        const int c = col_of(j);
-        x[j].x = (x[j].x - mean) * inv * g[c] + b[c];
-        x[j].y = (x[j].y - mean) * inv * g[c + 1] + b[c + 1];
+        x[j].x = (x[j].x - mean) * inv * g[j].x + b[j].x;
+        x[j].y = (x[j].y - mean) * inv * g[j].y + b[j].y;
     }
 }
 
-// Waits for the slot holding LayerNorm vectors; `staged` is this thread's
-// hand-off result, folded in so that an abort is taken uniformly.
-__device__ __forceinline__ const float* ln_slot_wait(Ctx& cx, bool staged, bool& abort, int where) {
-    bool ok;
-    const float* slot = slot_wait(cx, ok, where);
-    abort = csync_or(!ok || !staged);
-    return slot;
+// A LayerNorm's gamma and beta at this lane's GEMV columns, loaded into
+// registers when a phase starts waiting for its input (they do not depend on it).
+__device__ __forceinline__ void ln_load(const float* g, const float* b, float2 (&gv)[kVec], float2 (&bv)[kVec]) {
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        const int c = col_of(j);
+        gv[j] = __ldg(reinterpret_cast<const float2*>(g + c));
+        bv[j] = __ldg(reinterpret_cast<const float2*>(b + c));
+    }
 }
+
 
 // Slots per phase and CTA for grids of 129..148 CTAs (the host requires
 // ceil(8194 / grid) <= 64): c_attn 30 rows, c_proj 10, c_fc 40, mlp.c_proj 10
@@ -717,14 +716,14 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint3
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.q0, nrows = cx.rows.q1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.layer[li].b_qkv + r0 + t) : 0.f;  // used after the last slot
+    const LayerW& lw = cx.w.layer[li];
+    float2 gv[kVec], bv[kVec];
+    ln_load(lw.ln1_g, lw.ln1_b, gv, bv);
     const bool staged = stage_resid(a, cx.w, li, epoch, token, pos, cx.sm.xin, 10 + li);  // kept for phase C
-    bool abort;
-    const float* slot = ln_slot_wait(cx, staged, abort, 10 + li);
-    if (abort) return false;
+    if (csync_or(!staged)) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
-    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
-    slot_release(cx);
+    layernorm2(x, gv, bv, cx.sm.wstat);
     unsigned long long* out = a.b.qkv + r0;
     return gemv_slots<kSlotsQkv>(cx, nrows, x, 40 + li, [&](int row, float v) { put_tagged(out + row, epoch, v + bias); });
 }
@@ -914,14 +913,14 @@ __device__ bool phase_fc(Ctx& cx, int li, uint32_t epoch) {
     const DecodeArgs& a = cx.a;
     const int f0 = cx.rows.f0, nf = cx.rows.f1 - f0, t = threadIdx.x;
     const float bias = t < nf ? __ldg(cx.w.layer[li].b_fc + f0 + t) : 0.f;
+    const LayerW& lw = cx.w.layer[li];
+    float2 gv[kVec], bv[kVec];
+    ln_load(lw.ln2_g, lw.ln2_b, gv, bv);
     const bool staged = stage_tagged(a.b.hm, epoch, cx.sm.xin, a.b.ctl->status, 100 + li);
-    bool abort;
-    const float* slot = ln_slot_wait(cx, staged, abort, 100 + li);
-    if (abort) return false;
+    if (csync_or(!staged)) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
-    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
-    slot_release(cx);
+    layernorm2(x, gv, bv, cx.sm.wstat);
     float* out = a.b.f + f0;
     if (!gemv_slots<kSlotsFc>(cx, nf, x, 130 + li, [&](int row, float v) { out[row] = gelu_ref(v + bias); }))
         return false;
@@ -982,18 +981,16 @@ __device__ bool phase_head(Ctx& cx, uint32_t epoch, uint32_t token, uint32_t pos
     const DecodeArgs& a = cx.a;
     const int t = threadIdx.x, r0 = cx.rows.h0, nrows = cx.rows.h1 - r0;
     const float bias = t < nrows ? __ldg(cx.w.b_head + r0 + t) : 0.f;
+    float2 gv[kVec], bv[kVec];
+    ln_load(cx.w.lnf_g, cx.w.lnf_b, gv, bv);
     const bool staged = stage_resid(a, cx.w, cx.w.layers, epoch + 1, token, pos, cx.sm.xin, 200);
-    bool abort;
-    const float* slot = ln_slot_wait(cx, staged, abort, 200);
-    if (abort) return false;
+    if (csync_or(!staged)) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
-    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
-    slot_release(cx);
-    slot = ln_slot_wait(cx, true, abort, 200);
-    if (abort) return false;
-    layernorm2(x, slot, slot + kWidth, cx.sm.wstat);
-    slot_release(cx);
+    layernorm2(x, gv, bv, cx.sm.wstat);
+    ln_load(cx.w.fn_g, cx.w.fn_b, gv, bv);
+    csync();  // the next LayerNorm reuses wstat
+    layernorm2(x, gv, bv, cx.sm.wstat);
     float* out = a.b.logits + r0;
     return gemv_slots<kSlotsHead>(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
 }
@@ -1130,12 +1127,12 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phas
     if (threadIdx.x >= kThreads) {  // producer warp: exactly this phase's slots
         if (threadIdx.x == kThreads) {
             // segments of this phase (see seg_of)
-            int k0 = 6 * li, k1 = 6 * li;
-            if (phase == kPhQkv) k1 = k0 + 2;
-            else if (phase == kPhOproj) k0 += 2, k1 = k0 + 1;
-            else if (phase == kPhFc) k0 += 3, k1 = k0 + 2;
-            else if (phase == kPhMp) k0 += 5, k1 = k0 + 1;
-            else if (phase == kPhHead) k0 = 6 * sm.w.layers, k1 = k0 + 3;
+            int k0 = kSegsPerLayer * li, k1 = k0;
+            if (phase == kPhQkv) k1 = k0 + 1;
+            else if (phase == kPhOproj) k0 += 1, k1 = k0 + 1;
+            else if (phase == kPhFc) k0 += 2, k1 = k0 + 1;
+            else if (phase == kPhMp) k0 += 3, k1 = k0 + 1;
+            else if (phase == kPhHead) k0 = kSegsPerLayer * sm.w.layers, k1 = k0 + 1;
             if (k1 > k0) producer(a, sm.w, sm.ring, rows, k0, k1, 1);
             else sm.ring.producer_done = 1;
         }

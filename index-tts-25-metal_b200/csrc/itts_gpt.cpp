@@ -224,10 +224,6 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
                                  "mlp.c_fc.weight", "mlp.c_fc.bias", "mlp.c_proj.weight", "mlp.c_proj.bias"};
     for (uint32_t i = 0; i < layers; ++i)
         for (const char* n : per_layer) idx.push_back(add("gpt.gpt.h." + std::to_string(i) + "." + n));
-    // the decode's [gamma, beta] packs: two per layer, two for the head
-    const size_t kRow = size_t(1280) * 4;
-    const size_t pack_off = total;
-    total += (size_t(layers) + 1) * 4 * kRow;
     c->d_weights = dev_alloc<char>(total, "weight allocation");
     c->weight_bytes = total;
 
@@ -289,20 +285,6 @@ void upload_weights(itts_gpt_ctx* c, const itts::Mit2Bundle& b) {
         L.w_mp = ptr(o + 10);
         L.b_mp = ptr(o + 11);
     }
-    // fill the [gamma, beta] packs (device-to-device copies of the uploaded vectors)
-    char* packs = c->d_weights + pack_off;
-    auto put = [&](char* dst, const float* g, const float* b) {
-        ck(cudaMemcpy(dst, g, kRow, cudaMemcpyDeviceToDevice), "pack copy");
-        ck(cudaMemcpy(dst + kRow, b, kRow, cudaMemcpyDeviceToDevice), "pack copy");
-        return reinterpret_cast<const float*>(dst);
-    };
-    for (uint32_t i = 0; i < layers; ++i) {
-        itts::LayerW& L = c->hw.layer[i];
-        L.ln1_pack = put(packs + size_t(i) * 4 * kRow, L.ln1_g, L.ln1_b);
-        L.ln2_pack = put(packs + (size_t(i) * 4 + 2) * kRow, L.ln2_g, L.ln2_b);
-    }
-    c->hw.head_pack1 = put(packs + size_t(layers) * 4 * kRow, c->hw.lnf_g, c->hw.lnf_b);
-    c->hw.head_pack2 = put(packs + (size_t(layers) * 4 + 2) * kRow, c->hw.fn_g, c->hw.fn_b);
     // algorithmic bytes streamed per decode step: matrices, biases, LayerNorms,
     // mel_head and its bias, the final LayerNorms, two embedding rows
     const uint64_t mat_elems = 19660800ull * layers + 10488320ull;

@@ -30,8 +30,6 @@ struct LayerW {
     const float *ln2_g, *ln2_b;
     const float *w_fc, *b_fc;    // [5120, 1280]
     const float *w_mp, *b_mp;    // [1280, 5120]
-    // Contiguous [gamma, beta] copies of ln_1 and ln_2, one bulk copy each.
-    const float *ln1_pack, *ln2_pack;
 };
 
 struct ModelW {
@@ -41,8 +39,6 @@ struct ModelW {
     const float *fn_g, *fn_b;    // gpt.final_norm
     const float *w_head, *b_head;  // gpt.mel_head [8194, 1280] (nn.Linear layout)
     const float *mel_emb, *mel_pos;
-    // [ln_f gamma, beta], [final_norm gamma, beta]
-    const float *head_pack1, *head_pack2;
 };
 
 // Sampling options after GenerationOptions validation (gpt_sampling.cpp:168-173).
