@@ -730,8 +730,8 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint3
 
 // Split-K attention for the current query over keys [0, S] (S cached + the
 // current key), kernels.metal:2064-2145.  Unit = (head, chunk of ch keys);
-// warp w takes keys w, w+16, ... of the chunk with an online softmax (K and V
-// fetched together); the 16 warp states are merged into one partial (max,
+// warp w takes keys w, w+16, ... of the chunk with an online softmax over
+// blocks of 8 keys (their K and V rows fetched together); the 16 warp states are merged into one partial (max,
 // sum, 64 outputs).  The unit holding key S appends this token's K/V to the
 // cache.  A per-head arrival counter (acq_rel) finds the last unit of a head,
 // which merges the head's partials and hands the 64 outputs on as tagged
@@ -761,11 +761,12 @@ __device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
         const float2 q = *reinterpret_cast<const float2*>(qkv + 2 * lane);
         float m = -INFINITY, l = 0.f;
         float2 o = make_float2(0.f, 0.f);
-        for (uint32_t kb = k0 + warp; kb < k1; kb += 4 * kWarps) {
-            float2 kv[4], vv[4];
-            float s4[4];
+        constexpr int kKB = 8;  // keys per warp per online-softmax block: all their K/V loads in flight at once
+        for (uint32_t kb = k0 + warp; kb < k1; kb += kKB * kWarps) {
+            float2 kv[kKB], vv[kKB];
+            float sk[kKB];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < kKB; ++i) {
                 const uint32_t kk = kb + i * kWarps;
                 if (kk < k1) {
                     if (kk < S) {
@@ -780,24 +781,24 @@ __device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) s4[i] = fmaf(q.x, kv[i].x, q.y * kv[i].y);
+            for (int i = 0; i < kKB; ++i) sk[i] = fmaf(q.x, kv[i].x, q.y * kv[i].y);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) s4[i] += __shfl_xor_sync(0xffffffffu, s4[i], off);
+                for (int i = 0; i < kKB; ++i) sk[i] += __shfl_xor_sync(0xffffffffu, sk[i], off);
             float mn = m;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                s4[i] = kb + i * kWarps < k1 ? s4[i] * 0.125f : -INFINITY;  // rsqrt(64)
-                mn = fmaxf(mn, s4[i]);
+            for (int i = 0; i < kKB; ++i) {
+                sk[i] = kb + i * kWarps < k1 ? sk[i] * 0.125f : -INFINITY;  // rsqrt(64)
+                mn = fmaxf(mn, sk[i]);
             }
             const float corr = expf(m - mn);
             l *= corr;
             o.x *= corr;
             o.y *= corr;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float p = expf(s4[i] - mn);
+            for (int i = 0; i < kKB; ++i) {
+                const float p = expf(sk[i] - mn);
                 l += p;
                 o.x = fmaf(p, vv[i].x, o.x);
                 o.y = fmaf(p, vv[i].y, o.y);
