@@ -371,6 +371,7 @@ struct Ctx {
     int cta, ncta;
     uint32_t k;       // slots consumed so far (uniform across the consumers)
     bool resident;    // persistent kernel: sm.xin survives from phase A to phase C
+    const uint32_t* seen;  // persistent generate loop: the sampler's history set (else null)
 };
 
 // Every consumer thread waits for the next slot; `ok` is warp-uniform.
@@ -993,7 +994,14 @@ __device__ bool phase_head(Ctx& cx, uint32_t epoch, uint32_t token, uint32_t pos
     csync();  // the next LayerNorm reuses wstat
     layernorm2(x, gv, bv, cx.sm.wstat);
     float* out = a.b.logits + r0;
-    return gemv_slots<kSlotsHead>(cx, nrows, x, 201, [&](int row, float v) { out[row] = v + bias; });
+    // in the persistent generate loop the logits feed only the next draw: the
+    // repetition penalty and temperature are applied here, one logit per thread,
+    // instead of serially per thread of the sampler (sample_next passes scaled)
+    const uint32_t* seen = cx.seen;
+    return gemv_slots<kSlotsHead>(cx, nrows, x, 201, [&](int row, float v) {
+        const float s = v + bias;
+        out[row] = seen ? score_scale(s, uint32_t(r0 + row), seen, a.opts) : s;
+    });
 }
 
 // Grid barrier of the persistent kernel (all CTAs co-resident by the
@@ -1051,7 +1059,8 @@ __device__ bool forward_step(Ctx& cx, int step, uint32_t token, uint32_t pos, ui
 // The sampler in its own frame, so its registers do not constrain the phases.
 __device__ __noinline__ uint32_t sample_next(const float* logits, SampleOpts o, uint32_t i, SamplerSmem& sa,
                                              SamplerBig* big, int* status) {
-    return run_sampler(logits, o, i, o.do_sample == 0, sa, big, nullptr, status);
+    // draw 0 reads the prefill's raw logits; later draws read the head's scaled scores
+    return run_sampler(logits, o, i, o.do_sample == 0, sa, big, nullptr, status, i > 0);
 }
 
 constexpr int kCtaThreads = kThreads + 32;  // 16 consumer warps + the producer warp
@@ -1076,7 +1085,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_decode(DecodeArgs a) {
         return;
     }
     sampler_init_seen(sm.sa, a.history, a.history_n);
-    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, true};
+    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, true, a.mode == kModeGenerate ? sm.sa.seen : nullptr};
     SamplerBig* big = a.b.sampler_big + cta;
     unsigned target = 0;
     uint32_t token = a.first_code, n_codes = 0, stopped = 0, fwd = 0;
@@ -1140,7 +1149,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_phase(DecodeArgs a, int phas
         return;
     }
     const uint32_t token = *reinterpret_cast<volatile uint32_t*>(&a.b.ctl->token);
-    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, false};
+    Ctx cx{a, sm.w, sm.ring, sm.ph, rows, cta, ncta, 0, false, nullptr};
     switch (phase) {
         case kPhQkv: phase_qkv(cx, li, epoch, token, pos, S); break;
         case kPhAttn: phase_attn(cx, li, epoch, S); break;

@@ -106,6 +106,15 @@ __device__ __forceinline__ double uniform_at(int rng, uint64_t seed, uint64_t dr
 
 __device__ __forceinline__ bool bit_get(const uint32_t* b, uint32_t i) { return (b[i >> 5] >> (i & 31)) & 1u; }
 
+// The first two processors for one logit: repetition penalty (negative scores
+// multiplied, others divided) when token i was seen, then the temperature, in
+// the order and float arithmetic of run_sampler.
+__device__ __forceinline__ float score_scale(float s, uint32_t i, const uint32_t* seen, const SampleOpts& o) {
+    if (o.rp != 1.0f && bit_get(seen, i)) s = s < 0.0f ? s * o.rp : s / o.rp;
+    if (o.temperature != 1.0f) s = s / o.temperature;
+    return s;
+}
+
 // Seeds the repetition-penalty set with `hist` (tokens >= 8194 are ignored,
 // gpt_sampling.cpp:38-40).
 __device__ inline void sampler_init_seen(SamplerSmem& sm, const uint32_t* hist, uint32_t n) {
@@ -291,9 +300,12 @@ __device__ inline uint32_t block_argmax(const float (&s)[kPer], int base, int cn
 
 // Runs the processors on `logits` and, unless `out_scores` is given, selects a
 // token.  Returns the token, or 0xffffffff after setting `status` when the
-// reference would throw.  Must be called by all threads of the CTA.
+// reference would throw.  Must be called by all threads of the CTA.  With
+// `scaled` the scores already carry the repetition penalty and the temperature
+// (applied elementwise where they were produced, score_scale below).
 __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o, uint64_t draw, bool greedy,
-                                       SamplerSmem& sm, SamplerBig* big, float* out_scores, int* status) {
+                                       SamplerSmem& sm, SamplerBig* big, float* out_scores, int* status,
+                                       bool scaled = false) {
     const int tid = threadIdx.x;
     const int base = elem_base(), cnt = elem_cnt();
     float s[kPer];
@@ -315,12 +327,12 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
     }
 
     // repetition penalty (unique history; negative scores are multiplied)
-    if (o.rp != 1.0f) {
+    if (!scaled && o.rp != 1.0f) {
 #pragma unroll
         for (int k = 0; k < kPer; ++k)
             if (k < cnt && bit_get(sm.seen, base + k)) s[k] = s[k] < 0.0f ? s[k] * o.rp : s[k] / o.rp;
     }
-    if (o.temperature != 1.0f) {
+    if (!scaled && o.temperature != 1.0f) {
 #pragma unroll
         for (int k = 0; k < kPer; ++k) s[k] = s[k] / o.temperature;
     }
