@@ -10,7 +10,8 @@
 //   C    attn -> this CTA's attn.c_proj rows + bias + residual -> hm
 //   D    hm -> LN2 -> this CTA's c_fc rows + GELU -> f
 //   E    f -> this CTA's mlp.c_proj rows (5120 wide) + bias + residual -> h
-//   head h -> ln_f -> final_norm -> mel_head rows -> logits
+//   head h -> ln_f -> final_norm -> mel_head rows -> logits (in the generate
+//        loop already carrying the repetition penalty and the temperature)
 // Activations pass between CTAs as epoch-tagged 64-bit words that the reader
 // polls (the data is its own flag), f through a per-layer arrival counter; the
 // only grid barrier of a step follows the head.
