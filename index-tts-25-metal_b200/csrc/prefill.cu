@@ -43,41 +43,52 @@ __global__ void __launch_bounds__(256) k_ln_rows(const float* __restrict__ x, co
 enum GemmEpi : int { kEpiBias = 0, kEpiGelu = 1, kEpiResid = 2 };
 
 // W is fp32, or bf16 when WB (widened to fp32 on load: bf16 is the high half
-// of an fp32 word).
+// of an fp32 word).  64x64 output tile, 4x4 per thread, k-tiles of 32 (K must
+// be a multiple of 32): the next tile's global loads are in flight while the
+// current one is multiplied, and 32 k-steps per tile cover most of their L2
+// latency.  Each output sums its K products in k order.
 template <int EPI, bool WB>
 __global__ void __launch_bounds__(256) k_gemm_nt(const float* __restrict__ A, const void* __restrict__ Wv,
                                                  const float* __restrict__ bias, const float* __restrict__ R,
                                                  float* __restrict__ C, int M, int N, int K) {
-    constexpr int BM = 64, BN = 64, BK = 16;
+    constexpr int BM = 64, BN = 64, BK = 32;
     __shared__ __align__(16) float As[2][BK][BM + 4];
     __shared__ __align__(16) float Ws[2][BK][BN + 4];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int lr = tid >> 2, lk = (tid & 3) * 4;
-    float4 ra, rw;
+    const int lr = tid >> 2, lk = (tid & 3) * 4;  // and lk + 16
+    float4 ra[2], rw[2];
     auto gload = [&](int k0) {
-        ra = (m0 + lr < M) ? *reinterpret_cast<const float4*>(A + (size_t)(m0 + lr) * K + k0 + lk)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (n0 + lr >= N) {
-            rw = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else if (WB) {
-            const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(Wv) +
-                                                                 (size_t)(n0 + lr) * K + k0 + lk));
-            rw = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
-                             __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
-        } else {
-            rw = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(Wv) + (size_t)(n0 + lr) * K + k0 + lk));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int kk = k0 + lk + 16 * h;
+            ra[h] = (m0 + lr < M) ? *reinterpret_cast<const float4*>(A + (size_t)(m0 + lr) * K + kk)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (n0 + lr >= N) {
+                rw[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else if (WB) {
+                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(Wv) +
+                                                                     (size_t)(n0 + lr) * K + kk));
+                rw[h] = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                                    __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+            } else {
+                rw[h] = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(Wv) + (size_t)(n0 + lr) * K + kk));
+            }
         }
     };
     auto sstore = [&](int buf) {
-        As[buf][lk + 0][lr] = ra.x;
-        As[buf][lk + 1][lr] = ra.y;
-        As[buf][lk + 2][lr] = ra.z;
-        As[buf][lk + 3][lr] = ra.w;
-        Ws[buf][lk + 0][lr] = rw.x;
-        Ws[buf][lk + 1][lr] = rw.y;
-        Ws[buf][lk + 2][lr] = rw.z;
-        Ws[buf][lk + 3][lr] = rw.w;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int kk = lk + 16 * h;
+            As[buf][kk + 0][lr] = ra[h].x;
+            As[buf][kk + 1][lr] = ra[h].y;
+            As[buf][kk + 2][lr] = ra[h].z;
+            As[buf][kk + 3][lr] = ra[h].w;
+            Ws[buf][kk + 0][lr] = rw[h].x;
+            Ws[buf][kk + 1][lr] = rw[h].y;
+            Ws[buf][kk + 2][lr] = rw[h].z;
+            Ws[buf][kk + 3][lr] = rw[h].w;
+        }
     };
     float acc[4][4];
 #pragma unroll
@@ -211,6 +222,7 @@ cudaError_t launch_gemm_tc(int epi, bool wbf16, const float* A, const void* W, c
 // accumulation, even drained every 256 K, leaves prefill logits about 3x
 // further from the reference (8e-6 vs 3e-6 max_abs on the 24-layer model),
 // enough to change a 1024-code sampled run that the fp32 path reproduces.
+static_assert(kWidth % 32 == 0 && kFfn % 32 == 0, "k_gemm_nt k-tiles of 32");
 template <int EPI>
 static void gemm(const float* A, const float* W, bool wb, const float* bias, const float* R, float* C, int M, int N,
                  int K, int* status, cudaStream_t s) {
