@@ -177,20 +177,34 @@ int itts_gpt_sync(itts_gpt_ctx* ctx);
 int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode);
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx);
 
+/* ---- failure detection -------------------------------------------------------
+ * Every device-side wait of the decode kernels (weight-ring slots, hand-off
+ * polls, arrival counters, the grid barrier) gives up after a time limit and
+ * records a status that the next host check turns into ITTS_ERR_DEVICE_TIMEOUT
+ * (the reference throws std::runtime_error on a failed command buffer,
+ * metal_context.mm:4624-4626).  itts_gpt_set_wait_limit sets that limit for
+ * later decode launches of the context (0: the default of 2 s).
+ * itts_gpt_wait_probe runs one decode phase that waits for a hand-off no phase
+ * publishes, so it ends at the limit and returns ITTS_ERR_DEVICE_TIMEOUT; the
+ * context stays usable.  No counterpart in the reference. */
+int itts_gpt_set_wait_limit(itts_gpt_ctx* ctx, uint64_t ns);
+int itts_gpt_wait_probe(itts_gpt_ctx* ctx);
+
 /* ---- allocation-free processors --------------------------------------------
  * No counterpart in the reference.  The logits processors of
  * itts_gpt_apply_processors for callers that cannot allocate device memory:
- * a thread inside a CUDA stream capture (allocation is illegal there), a
- * latency-critical serving thread (cudaMalloc/cudaFree can synchronise the
- * device) or a process whose device memory is fully reserved elsewhere.  It
- * needs no context and calls no cudaMalloc/cudaFree: inputs and outputs are
- * host arrays staged through one static device array of 133,136 bytes that
- * every GPU loading this library holds until exit.  history_n is limited to
- * 16384 tokens (larger values return ITTS_ERR_INVALID_ARGUMENT).  The first
- * call on a device looks up that array's address; make it before any stream
- * capture.  All calls share the array: calls that overlap on one GPU (from two
- * host threads) race, so serialise them.  Errors are reported by
- * itts_gpt_last_error(NULL) on the calling thread. */
+ * a latency-critical serving thread (cudaMalloc/cudaFree can synchronise the
+ * whole device) or a process whose device memory is fully reserved by another
+ * allocator.  It needs no context and calls no cudaMalloc/cudaFree: inputs and
+ * outputs are host arrays staged through one static device array of 133,136
+ * bytes that every GPU loading this library holds until exit.  The call is
+ * synchronous (blocking copies in, one kernel, blocking copies out).
+ * history_n is limited to 16384 tokens (larger values return
+ * ITTS_ERR_INVALID_ARGUMENT).  The first call on a device looks up that
+ * array's address; make it before any stream capture.  All calls share the
+ * array: calls that overlap on one GPU (from two host threads) race, so
+ * serialise them.  Errors are reported by itts_gpt_last_error(NULL) on the
+ * calling thread. */
 int itts_gpt_apply_processors_noalloc(int device, const float* logits, size_t n, const uint32_t* history,
                                       size_t history_n, const itts_gen_opts* opts, float* out);
 

@@ -189,15 +189,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // or error.
 constexpr unsigned long long kStatusPollNs = 200000ull;
 
-__device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, int* status, int where) {
+// Time limit of the launch's waits: DecodeArgs::wait_ns, or kWaitLimitNs when 0.
+__device__ __forceinline__ unsigned long long wait_limit(const DecodeArgs& a) {
+    return a.wait_ns ? a.wait_ns : kWaitLimitNs;
+}
+
+__device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, const DecodeArgs& a, int where) {
     if (mbar_try_wait(bar, parity)) return true;
+    int* status = a.b.ctl->status;
     const unsigned long long t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0) {
             const unsigned long long dt = globaltimer_ns() - t0;
             if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
-            if (dt > kWaitLimitNs) {
+            if (dt > wait_limit(a)) {
                 set_status(status, kStatusRingTimeout, where, (int)i);
                 return false;
             }
@@ -270,9 +276,10 @@ __device__ __forceinline__ bool pf_advance(const ModelW& w, const Rows& rows, in
 // Bounded wait of the producer for a slot's previous use to be handed back;
 // while it waits it keeps the L2 prefetch kPfAhead bytes ahead of the ring.
 // False when the consumers raised `stop`, on an error status or on timeout.
-__device__ bool wait_empty(Ring& R, int s, uint32_t parity, int* status, uint32_t j, const ModelW& w,
+__device__ bool wait_empty(Ring& R, int s, uint32_t parity, const DecodeArgs& a, uint32_t j, const ModelW& w,
                            const Rows& rows, int k0, int k1, int n_steps, PfCursor& pf, unsigned long long issued) {
     if (mbar_try_wait(&R.empty[s], parity)) return true;
+    int* status = a.b.ctl->status;
     const unsigned long long t0 = globaltimer_ns();
     bool more = true;
     for (uint32_t i = 1;; ++i) {
@@ -285,7 +292,7 @@ __device__ bool wait_empty(Ring& R, int s, uint32_t parity, int* status, uint32_
             if (R.stop) return false;
             const unsigned long long dt = globaltimer_ns() - t0;
             if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
-            if (dt > kWaitLimitNs) {
+            if (dt > wait_limit(a)) {
                 set_status(status, kStatusRingTimeout, 900, (int)j);
                 return false;
             }
@@ -298,7 +305,6 @@ __device__ bool wait_empty(Ring& R, int s, uint32_t parity, int* status, uint32_
 // use to be handed back before reusing it and for the copy kInFlight slots
 // back to have landed before issuing the next.
 __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Rows& rows, int k0, int k1, int n_steps) {
-    int* status = a.b.ctl->status;
     uint32_t j = 0, parity = 0;
     int s = 0;
     unsigned long long issued = 0;  // schedule bytes issued into the ring
@@ -313,10 +319,10 @@ __device__ void producer(const DecodeArgs& a, const ModelW& w, Ring& R, const Ro
                 const uint32_t n = min(bytes - off, (uint32_t)kSlotBytes);
                 if (j >= kInFlight) {  // that slot is still in the ring (kInFlight < kSlots)
                     const uint32_t jp = j - kInFlight;
-                    if (!mbar_wait_bounded(&R.full[jp % kSlots], (jp / kSlots) & 1u, status, 901)) goto done;
+                    if (!mbar_wait_bounded(&R.full[jp % kSlots], (jp / kSlots) & 1u, a, 901)) goto done;
                 }
                 if (j >= kSlots &&
-                    !wait_empty(R, s, parity ^ 1u, status, j, w, rows, k0, k1, n_steps, pf, issued))
+                    !wait_empty(R, s, parity ^ 1u, a, j, w, rows, k0, k1, n_steps, pf, issued))
                     goto done;
                 mbar_expect_tx(&R.full[s], n);
                 bulk_g2s(R.data[s], p + off, n, &R.full[s], policy);
@@ -378,7 +384,7 @@ struct Ctx {
 // Every consumer thread waits for the next slot; `ok` is warp-uniform.
 __device__ __forceinline__ const float* slot_wait(Ctx& cx, bool& ok, int where) {
     const int s = cx.k % kSlots;
-    ok = mbar_wait_bounded(&cx.R.full[s], (cx.k / kSlots) & 1u, cx.a.b.ctl->status, where);
+    ok = mbar_wait_bounded(&cx.R.full[s], (cx.k / kSlots) & 1u, cx.a, where);
     ok = __all_sync(0xffffffffu, ok);
     return reinterpret_cast<const float*>(cx.R.data[s]);
 }
@@ -594,7 +600,9 @@ __device__ __forceinline__ float tagged_value(unsigned long long w) { return __u
 
 // Polls words p[0..2n) (n 16-byte pairs from p, stride 2) until all carry
 // `epoch`; bounded like every wait (false on timeout or an error status).
-__device__ bool poll_tagged(const unsigned long long* p, int n, uint32_t epoch, float* out, int* status, int where) {
+__device__ bool poll_tagged(const unsigned long long* p, int n, uint32_t epoch, float* out, const DecodeArgs& a,
+                            int where) {
+    int* status = a.b.ctl->status;
     ulonglong2 v[2];
     for (int i = 0; i < n; ++i) v[i] = ld_tagged2(p + 2 * i);
     unsigned long long t0 = 0;
@@ -606,7 +614,7 @@ __device__ bool poll_tagged(const unsigned long long* p, int n, uint32_t epoch, 
         if ((it & 15u) == 15u) {
             const unsigned long long dt = globaltimer_ns() - t0;
             if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
-            if (dt > kWaitLimitNs) {
+            if (dt > wait_limit(a)) {
                 set_status(status, kStatusBarrierTimeout, where, (int)epoch);
                 return false;
             }
@@ -623,12 +631,12 @@ __device__ bool poll_tagged(const unsigned long long* p, int n, uint32_t epoch, 
 
 // Stages a tagged 1280-vector in shared memory (threads < 320, four words
 // each); the caller's next consumer barrier publishes it.  False on abort.
-__device__ __forceinline__ bool stage_tagged(const unsigned long long* src, uint32_t epoch, float* dst, int* status,
-                                             int where) {
+__device__ __forceinline__ bool stage_tagged(const unsigned long long* src, uint32_t epoch, float* dst,
+                                             const DecodeArgs& a, int where) {
     const int t = threadIdx.x;
     if (t >= kWidth / 4) return true;
     float v[4];
-    if (!poll_tagged(src + 4 * t, 2, epoch, v, status, where)) return false;
+    if (!poll_tagged(src + 4 * t, 2, epoch, v, a, where)) return false;
     *reinterpret_cast<float4*>(dst + 4 * t) = make_float4(v[0], v[1], v[2], v[3]);
     return true;
 }
@@ -648,7 +656,7 @@ __device__ __forceinline__ bool stage_resid(const DecodeArgs& a, const ModelW& w
         const float4 p = __ldg(reinterpret_cast<const float4*>(w.mel_pos + (size_t)pos * kWidth) + t);
         reinterpret_cast<float4*>(dst)[t] = make_float4(e.x + p.x, e.y + p.y, e.z + p.z, e.w + p.w);
     } else {
-        return stage_tagged(a.b.h, epoch - 1, dst, a.b.ctl->status, where);
+        return stage_tagged(a.b.h, epoch - 1, dst, a, where);
     }
     return true;
 }
@@ -740,7 +748,6 @@ __device__ bool phase_qkv(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint3
 // words; the others go straight on to phase C.
 __device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
     const DecodeArgs& a = cx.a;
-    int* status = a.b.ctl->status;
     const uint32_t keys = S + 1;
     const uint32_t ch = attn_chunk(keys, cx.ncta);
     const uint32_t nch = (keys + ch - 1) / ch, units = kHeads * nch;
@@ -754,7 +761,7 @@ __device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
         if (t < 48) {  // q, k, v of head h: 3 x 16 threads x 4 words
             const int part = t >> 4, q4 = t & 15;
             float v[4];
-            ok = poll_tagged(a.b.qkv + part * kWidth + h * kHeadDim + 4 * q4, 2, epoch, v, status, 60 + li);
+            ok = poll_tagged(a.b.qkv + part * kWidth + h * kHeadDim + 4 * q4, 2, epoch, v, a, 60 + li);
             *reinterpret_cast<float4*>(qkv + part * kHeadDim + 4 * q4) = make_float4(v[0], v[1], v[2], v[3]);
         }
         if (csync_or(!ok)) return false;
@@ -882,7 +889,6 @@ __device__ bool phase_attn(Ctx& cx, int li, uint32_t epoch, uint32_t S) {
 
 __device__ bool phase_oproj(Ctx& cx, int li, uint32_t epoch, uint32_t token, uint32_t pos) {
     const DecodeArgs& a = cx.a;
-    int* status = a.b.ctl->status;
     const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0;
     const int t = threadIdx.x;
     float bias = 0.f, res = 0.f;  // used after the last slot
@@ -897,11 +903,11 @@ __device__ bool phase_oproj(Ctx& cx, int li, uint32_t epoch, uint32_t token, uin
         } else {
             const unsigned long long* hp = a.b.h + (r & ~1);
             float v[2];
-            ok = poll_tagged(hp, 1, epoch - 1, v, status, 70 + li);
+            ok = poll_tagged(hp, 1, epoch - 1, v, a, 70 + li);
             res = v[r & 1];
         }
     }
-    ok = ok && stage_tagged(a.b.attn, epoch, cx.sm.attn, status, 70 + li);
+    ok = ok && stage_tagged(a.b.attn, epoch, cx.sm.attn, a, 70 + li);
     if (csync_or(!ok)) return false;
     float2 x[kVec];
 #pragma unroll
@@ -919,7 +925,7 @@ __device__ bool phase_fc(Ctx& cx, int li, uint32_t epoch) {
     const LayerW& lw = cx.w.layer[li];
     float2 gv[kVec], bv[kVec];
     ln_load(lw.ln2_g, lw.ln2_b, gv, bv);
-    const bool staged = stage_tagged(a.b.hm, epoch, cx.sm.xin, a.b.ctl->status, 100 + li);
+    const bool staged = stage_tagged(a.b.hm, epoch, cx.sm.xin, a, 100 + li);
     if (csync_or(!staged)) return false;
     float2 x[kVec];
     gather_x(cx.sm.xin, x);
@@ -936,15 +942,16 @@ __device__ bool phase_fc(Ctx& cx, int li, uint32_t epoch) {
 
 // Thread 0: bounded wait until `*cnt` reaches `target` (acquire); false on
 // timeout or an error status.
-__device__ bool wait_count(const unsigned* cnt, unsigned target, int* status, int where) {
+__device__ bool wait_count(const unsigned* cnt, unsigned target, const DecodeArgs& a, int where) {
     if (ld_acquire_gpu(cnt) >= target) return true;
+    int* status = a.b.ctl->status;
     const unsigned long long t0 = globaltimer_ns();
     for (unsigned spins = 1;; ++spins) {
         if (ld_acquire_gpu(cnt) >= target) return true;
         if ((spins & 31u) == 0) {
             const unsigned long long dt = globaltimer_ns() - t0;
             if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
-            if (dt > kWaitLimitNs) {
+            if (dt > wait_limit(a)) {
                 set_status(status, kStatusBarrierTimeout, where, (int)target);
                 return false;
             }
@@ -955,19 +962,18 @@ __device__ bool wait_count(const unsigned* cnt, unsigned target, int* status, in
 // f -> this CTA's mlp.c_proj rows (the rows of its attn.c_proj block) -> h = hm + y + bias.
 __device__ bool phase_mp(Ctx& cx, int li, uint32_t epoch) {
     const DecodeArgs& a = cx.a;
-    int* status = a.b.ctl->status;
     const int r0 = cx.rows.o0, nrows = cx.rows.o1 - r0, t = threadIdx.x;
     float bias = 0.f, res = 0.f;
     bool ok = true;
     if (t < nrows) {
         bias = __ldg(cx.w.layer[li].b_mp + r0 + t);
         float v[2];
-        ok = poll_tagged(a.b.hm + ((r0 + t) & ~1), 1, epoch, v, status, 160 + li);
+        ok = poll_tagged(a.b.hm + ((r0 + t) & ~1), 1, epoch, v, a, 160 + li);
         res = v[(r0 + t) & 1];
     }
     if (t == 0) {
         const unsigned step = (epoch - 1) / unsigned(cx.w.layers);
-        ok = wait_count(&a.b.ctl->f_cnt[li], unsigned(cx.ncta) * (step + 1), status, 160 + li) && ok;
+        ok = wait_count(&a.b.ctl->f_cnt[li], unsigned(cx.ncta) * (step + 1), a, 160 + li) && ok;
     }
     if (csync_or(!ok)) return false;
     float2 x[kVec];
@@ -1027,7 +1033,7 @@ __device__ bool grid_barrier(Ctx& cx, unsigned& target, int where) {
                         abort = 1;
                         break;
                     }
-                    if (dt > kWaitLimitNs) {
+                    if (dt > wait_limit(cx.a)) {
                         set_status(status, kStatusBarrierTimeout, where, (int)target);
                         abort = 1;
                         break;
@@ -1205,6 +1211,15 @@ cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cud
 
 cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s) {
     k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhHead, 0, 0, 0, 0);
+    return cudaGetLastError();
+}
+
+// Layer 0's attn.c_proj phase for an epoch that no phase publishes: every CTA
+// polls the attention hand-off until the launch's wait limit, records a
+// timeout in the status word and returns (its ring drained).  Exercises the
+// device-timeout path with a wait nothing ends, without a fault or a hang.
+cudaError_t launch_wait_probe(const DecodeArgs& a, int ncta, cudaStream_t s) {
+    k_phase<<<ncta, kCtaThreads, sizeof(DecodeSmem), s>>>(a, kPhOproj, 0, 0x7fffffffu, 0, 0);
     return cudaGetLastError();
 }
 

@@ -108,6 +108,7 @@ struct itts_gpt_ctx {
     uint32_t cached = 0, prefix_rows = 0;
     bool have_prefill = false;
     uint64_t launches = 0;
+    unsigned long long wait_ns = 0;  // device wait limit of decode launches (0: the kernels' default)
     bool pending = false;           // an async decode has not been synced yet
     uint32_t* pending_info = nullptr;
 
@@ -381,6 +382,7 @@ itts::DecodeArgs decode_args(itts_gpt_ctx* c) {
     a.history = c->d_history;
     a.history_n = 2;
     a.codes = c->d_codes;
+    a.wait_ns = c->wait_ns;
     return a;
 }
 
@@ -1010,5 +1012,26 @@ int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode) {
 }
 
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int itts_gpt_set_wait_limit(itts_gpt_ctx* ctx, uint64_t ns) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    ctx->wait_ns = ns;
+    return ITTS_OK;
+}
+
+int itts_gpt_wait_probe(itts_gpt_ctx* ctx) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        reset_ctl(ctx);
+        ck(cudaMemsetAsync(ctx->db.qkv, 0, ctx->tagged_bytes, ctx->stream), "hand-off reset");
+        const itts::DecodeArgs a = decode_args(ctx);
+        ck(ctx->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_wait_probe(a, ctx->sm_count, ctx->stream)
+                                           : itts::wf32::launch_wait_probe(a, ctx->sm_count, ctx->stream),
+           "wait probe launch");
+        ++ctx->launches;
+        check_status(ctx);
+    });
+}
 
 }  // extern "C"

@@ -100,6 +100,7 @@ struct DecodeArgs {
     uint32_t* codes;      // kModeGenerate output [n_iter]
     uint32_t* info_out;   // optional copy of ctl->info (may be null)
     const float* head_src;  // prefill: last hidden row fed to the head phase
+    unsigned long long wait_ns;  // time limit of every device-side wait; 0: the default (2 s)
 };
 
 // ---- host-side launchers ----------------------------------------------------
@@ -112,6 +113,7 @@ struct DecodeArgs {
     cudaError_t launch_decode_layered(const DecodeArgs& a, int layers, int ncta, cudaStream_t s,               \
                                       uint64_t* launches);                                                     \
     cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s);                                    \
+    cudaError_t launch_wait_probe(const DecodeArgs& a, int ncta, cudaStream_t s);                              \
     }
 ITTS_DECLARE_DECODE_LAUNCHERS(wf32)
 ITTS_DECLARE_DECODE_LAUNCHERS(wbf16)

@@ -2,12 +2,15 @@
 // itts_gpt_apply_processors for callers that must not allocate device memory.
 //
 // Who needs it: code that runs where cudaMalloc/cudaFree are off limits --
-// a host thread that is inside a CUDA stream capture (allocation calls are
-// illegal there), a latency-critical serving thread (cudaMalloc and cudaFree
-// can synchronise the whole device), or a process whose device memory is
-// already fully reserved by another allocator.  The regular entry point stages
-// its inputs in buffers owned by a context and may grow its history buffer
-// with cudaMalloc; this one needs no context and allocates nothing.
+// a latency-critical serving thread (cudaMalloc and cudaFree can synchronise
+// the whole device and stall every stream on it), or a process whose device
+// memory is already fully reserved by another allocator (a serving framework's
+// memory pool that takes nearly all of HBM up front).  The regular entry point
+// stages its inputs in buffers owned by a context and may grow its history
+// buffer with cudaMalloc; this one needs no context and allocates nothing.
+// It is synchronous: it copies the inputs in, runs one kernel and copies the
+// scores back with blocking cudaMemcpy calls, and returns when they are on
+// the host.
 //
 // Scratch: one file-scope __device__ array (kNoAllocScratchBytes, below) that
 // every GPU loading this library holds until the process exits.  It stages the
@@ -129,9 +132,17 @@ extern "C" int itts_gpt_apply_processors_noalloc(int device, const float* logits
         if (ck(cudaGetLastError(), "processors launch") &&
             ck(cudaMemcpy(out, s->scores, kVocab * sizeof(float), cudaMemcpyDeviceToHost), "scores read") &&
             ck(cudaMemcpy(status, s->status, sizeof(status), cudaMemcpyDeviceToHost), "status read") && status[0]) {
+            // the device status codes the processors can raise, mapped as the
+            // context entry points map them (check_status in itts_gpt.cpp)
             rc = ITTS_ERR_RUNTIME;
-            msg = status[0] == kStatusZeroMass ? "GPT sampling probability mass is zero"
-                                               : "GPT top_p filtering removed all logits";
+            switch (status[0]) {
+                case kStatusNoFiniteLogits: msg = "GPT top_p filtering removed all logits"; break;
+                case kStatusZeroMass: msg = "GPT sampling probability mass is zero"; break;
+                default:
+                    msg = "device error " + std::to_string(status[0]) + " (site " + std::to_string(status[1]) +
+                          ", detail " + std::to_string(status[3]) + ")";
+                    break;
+            }
         }
     }
     cudaSetDevice(prev);

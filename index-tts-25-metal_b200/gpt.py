@@ -84,6 +84,8 @@ SIGNATURES = {
     "itts_gpt_sync": (C.c_int, [_P]),
     "itts_gpt_set_decode_mode": (C.c_int, [_P, C.c_int]),
     "itts_gpt_launch_count": (C.c_uint64, [_P]),
+    "itts_gpt_set_wait_limit": (C.c_int, [_P, C.c_uint64]),
+    "itts_gpt_wait_probe": (C.c_int, [_P]),
     "itts_gpt_apply_processors_noalloc": (C.c_int, [C.c_int, _P, C.c_size_t, _P, C.c_size_t, C.POINTER(GenOpts),
                                                     _P]),
 }
@@ -212,6 +214,15 @@ class GptDecoder:
     @property
     def launch_count(self) -> int:
         return self._lib.itts_gpt_launch_count(self._h)
+
+    def set_wait_limit(self, ns: int):
+        """Time limit of the decode kernels' device-side waits (0: default 2 s)."""
+        self._check(self._lib.itts_gpt_set_wait_limit(self._h, ns))
+
+    def wait_probe(self):
+        """Runs one phase whose wait nothing ends: raises GptError with
+        ERR_DEVICE_TIMEOUT once the wait limit passes."""
+        self._check(self._lib.itts_gpt_wait_probe(self._h))
 
     # -- GptDecoder interface
     def prepare(self, speaker, emotion, text, language: int) -> np.ndarray:

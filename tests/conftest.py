@@ -91,3 +91,21 @@ def latent_prefix(prepare, seed, n_latents, n_text, language=3):
     p = prepare(spk, emo, ids, language)
     lat = np.random.default_rng(seed + 1).standard_normal((n_latents, 1280)).astype(np.float32)
     return np.concatenate([lat, p[3:]], 0)
+
+
+def text_lengths(seed, n, lo=40, hi=300):
+    """Text lengths of configs[2] requests, uniform in [lo, hi] (as in
+    tests/golden/make_golden.py)."""
+    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+
+
+def config3_prefix(prepare, seed=3003, n_latents=32, n_emotion=16, n_text=400, language=3):
+    """n_latents N(0,1) conditioning rows, n_emotion N(0,1)
+    emotion-conditioning rows appended as rows, then prepare()'s text rows and
+    start row (32 + 16 + 402 + 1 = 451 rows), as in tests/golden/make_golden.py."""
+    spk, emo, ids = conditioning(seed, n_text)
+    p = prepare(spk, emo, ids, language)
+    r = np.random.default_rng(seed + 1)
+    lat = r.standard_normal((n_latents, 1280)).astype(np.float32)
+    emov = r.standard_normal((n_emotion, 1280)).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([lat, emov, p[3:]], 0))

@@ -18,6 +18,20 @@ Fixtures (all inputs seeded):
   processors.npz     apply_gpt_sampling_processors on seeded logits and history
                      for several option sets (src/main.cpp:147-158 layout:
                      [temperature, top_k, top_p, repetition_penalty, num_beams]).
+  gpt_config2_beam.npz   configs[2], beam half: 24-layer bundle (stop masked),
+                     32 latents + a text length drawn from U[40,300], greedy
+                     3-beam search (rp 10, length penalty 0), 600 codes.
+  gpt_config2_batch.npz  configs[2], batch half: 8 independent requests, text
+                     lengths from U[40,300], SplitMix64 sampled (T 0.8, k 30,
+                     p 0.8, rp 10, seeds 1234+i), 600 codes each.
+  gpt_config3.npz    configs[3], prefill-heavy: 32 latents + 16 N(0,1)
+                     emotion-conditioning rows + 400 text ids + start row = 451
+                     rows; prefill logits, two teacher-forced step logits and 128
+                     SplitMix64 sampled codes (seed 1234).
+  gpt_config1_philox.npz  configs[1] with the Philox4x32-10 stream (the
+                     benchmark's mode, seed 1234): 1024 sampled codes from the
+                     oracle port (the reference has only SplitMix64; the port
+                     reproduces every reference fixture bit for bit).
 """
 from __future__ import annotations
 
@@ -109,6 +123,86 @@ def make_long(ref_path, sha, out, n_codes):
     print("wrote", out)
 
 
+def text_lengths(seed, n, lo=40, hi=300):
+    """Text lengths of configs[2] requests, uniform in [lo, hi]."""
+    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+
+
+def make_config2_beam(ref_path, sha, out, n_codes):
+    ref = O.RefOracle(ref_path)
+    n_text = int(text_lengths(2002, 1)[0])
+    p, ids = latent_prefix(ref, 2002, 32, n_text)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 1, "bundle_sha256": sha,
+         "text": ids, "rows": np.uint32(p.shape[0]), "n_codes": np.uint32(n_codes)}
+    t = time.time()
+    c, s = ref.generate(p, O.make_opts(do_sample=False, num_beams=3), n_codes)
+    print("config2 beam", len(c), p.shape[0], time.time() - t, flush=True)
+    d["beam.codes"], d["beam.stopped"] = c, np.int32(s)
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+def make_config2_batch(ref_path, sha, out, n_codes, batch=8):
+    ref = O.RefOracle(ref_path)
+    lens = text_lengths(2100, batch)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 1, "bundle_sha256": sha,
+         "text_lengths": lens.astype(np.uint32), "n_codes": np.uint32(n_codes), "batch": np.uint32(batch)}
+    for i in range(batch):
+        p, ids = latent_prefix(ref, 2200 + i, 32, int(lens[i]))
+        t = time.time()
+        c, s = ref.generate(p, O.make_opts(seed=1234 + i), n_codes)
+        print("config2 batch", i, len(c), p.shape[0], time.time() - t, flush=True)
+        d[f"req{i}.text"], d[f"req{i}.rows"] = ids, np.uint32(p.shape[0])
+        d[f"req{i}.codes"] = c
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+def config3_prefix(prepare, seed=3003, n_latents=32, n_emotion=16, n_text=400, language=3):
+    """n_latents N(0,1) conditioning rows, then n_emotion N(0,1)
+    emotion-conditioning rows appended as rows, then prepare()'s text rows and
+    start row (32 + 16 + 402 + 1 = 451 rows)."""
+    spk, emo, ids = conditioning(seed, n_text)
+    p = prepare(spk, emo, ids, language)
+    r = np.random.default_rng(seed + 1)
+    lat = r.standard_normal((n_latents, 1280)).astype(np.float32)
+    emov = r.standard_normal((n_emotion, 1280)).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([lat, emov, p[3:]], 0)), ids
+
+
+def make_config3(ref_path, sha, out, n_codes=128):
+    ref = O.RefOracle(ref_path)
+    p, ids = config3_prefix(ref.prepare)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 1, "bundle_sha256": sha,
+         "text": ids, "rows": np.uint32(p.shape[0])}
+    t = time.time()
+    d["prefill.logits"] = ref.prefill(p)
+    print("config3 prefill", p.shape[0], time.time() - t, flush=True)
+    codes = np.array([311, 4242], np.uint32)
+    d["step.codes"] = codes
+    for i in range(2):
+        d[f"step.{i}.logits"] = ref.step(int(codes[i]), i + 2)
+    t = time.time()
+    c, s = ref.generate(p, O.make_opts(seed=1234), n_codes)
+    print("config3 sampled", len(c), time.time() - t, flush=True)
+    d["sampled.codes"] = c
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+def make_config1_philox(path, sha, out, n_codes):
+    port = O.PortOracle(path)
+    p, ids = latent_prefix(port, 1002, 32, 200)
+    d = {"bundle_seed": 42, "bundle_layers": 24, "bundle_mask_stop": 1, "bundle_sha256": sha,
+         "text": ids, "rows": np.uint32(p.shape[0])}
+    t = time.time()
+    c, s = port.generate(p, O.make_opts(seed=1234, rng=1), n_codes)
+    print("config1 philox", len(c), time.time() - t, flush=True)
+    d["philox.codes"] = c
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
 PROCESSOR_CASES = {
     # name: [temperature, top_k, top_p, repetition_penalty, num_beams]
     "standard": [0.8, 30, 0.8, 10.0, 1],
@@ -140,7 +234,9 @@ def make_processors(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["full", "long", "processors"], default=None)
+    ap.add_argument("--only", choices=["full", "long", "processors", "config2_beam", "config2_batch", "config3",
+                                       "config1_philox"], default=None)
+    ap.add_argument("--config2-codes", type=int, default=600)
     ap.add_argument("--long-codes", type=int, default=1024)
     a = ap.parse_args()
     if not O.RefOracle.available():
@@ -153,6 +249,18 @@ def main():
     if a.only in (None, "long"):
         path, sha = bundle(42, 24, True)
         make_long(path, sha, os.path.join(HERE, "gpt_long.npz"), a.long_codes)
+    if a.only in (None, "config3"):
+        path, sha = bundle(42, 24, True)
+        make_config3(path, sha, os.path.join(HERE, "gpt_config3.npz"))
+    if a.only in (None, "config1_philox"):
+        path, sha = bundle(42, 24, True)
+        make_config1_philox(path, sha, os.path.join(HERE, "gpt_config1_philox.npz"), a.long_codes)
+    if a.only in (None, "config2_beam"):
+        path, sha = bundle(42, 24, True)
+        make_config2_beam(path, sha, os.path.join(HERE, "gpt_config2_beam.npz"), a.config2_codes)
+    if a.only in (None, "config2_batch"):
+        path, sha = bundle(42, 24, True)
+        make_config2_batch(path, sha, os.path.join(HERE, "gpt_config2_batch.npz"), a.config2_codes)
 
 
 if __name__ == "__main__":

@@ -299,3 +299,26 @@ def test_errors_match_reference_and_leave_context_usable(dec_shallow, gpt_mod):
     # still usable
     r = dec_shallow.generate(prefix, G.gen_opts(do_sample=False), 4)
     assert len(r.codes) == 4
+
+
+def test_device_wait_timeout_returns_status_and_context_recovers(gpt_mod, port_shallow, shallow_bundle):
+    """The failure path of the bounded device waits: one decode phase waits
+    for an attention hand-off that no phase publishes.  With a 1 ms limit every
+    CTA gives up, the kernel records a timeout and returns (no fault, no hang),
+    and the call reports ERR_DEVICE_TIMEOUT.  The same context then decodes
+    normally with the default limit."""
+    import time
+    G = gpt_mod
+    with G.GptDecoder(shallow_bundle) as dec:
+        dec.set_wait_limit(1_000_000)
+        t0 = time.perf_counter()
+        with pytest.raises(G.GptError) as e:
+            dec.wait_probe()
+        assert e.value.status == G.ERR_DEVICE_TIMEOUT, e.value
+        assert "timed out" in e.value.message
+        assert time.perf_counter() - t0 < 5.0
+        dec.set_wait_limit(0)
+        prefix = np.random.default_rng(3).standard_normal((9, 1280)).astype(np.float32)
+        r = dec.generate(prefix, G.gen_opts(do_sample=False), 6)
+        e_codes, _ = port_shallow.generate(prefix, __import__("oracle").make_opts(do_sample=False), 6)
+        np.testing.assert_array_equal(r.codes, e_codes)
