@@ -133,13 +133,17 @@ int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, c
 
 /* ---- batch of independent requests ----------------------------------------
  * Request i is the prefix prefixes[i] (n_floats[i] floats) with options
- * opts[i]; each is prefilled and decoded exactly as itts_gpt_generate would,
- * one after another on the context's device.  Codes of request i go to
+ * opts[i].  Requests without beams are decoded together, up to 16 per group:
+ * each is prefilled into its own KV arena, then one batched forward step per
+ * token reads every weight once for all of them.  Each request's codes are
+ * exactly those itts_gpt_generate returns for it alone (same arithmetic per
+ * row).  Beam requests run one at a time.  Codes of request i go to
  * codes + i * max_tokens, its count to n_codes[i], its stop flag to
  * stopped[i].  Every request is validated before any runs.  No single call
  * of the reference corresponds: its server runs GptDecoder::generate once per
- * request (src/server.cpp:41-47); this is that loop behind one call.  The
- * context's cache holds the last request's state afterwards. */
+ * request (src/server.cpp:41-47); this is that loop behind one call.
+ * Afterwards the context holds no prefill (itts_gpt_step needs a new
+ * itts_gpt_prefill); the same holds after a beam-search generate. */
 int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const* prefixes, const size_t* n_floats,
                             const itts_gen_opts* opts, uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes,
                             int* stopped);
@@ -176,6 +180,20 @@ int itts_gpt_sync(itts_gpt_ctx* ctx);
  * phase, same device code).  Counters: kernel launches issued by the context. */
 int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode);
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx);
+
+/* Device time of the last itts_gpt_generate / itts_gpt_generate_batch call,
+ * from CUDA events on the context's stream: the prefill(s), then the token
+ * loop (for beam search including the host's candidate choice between
+ * steps).  forward_steps counts decode forward steps (batched steps count
+ * once for all their rows); rows is the largest number of rows per step.
+ * No counterpart in the reference (its timing is per command buffer). */
+typedef struct itts_gpt_timing {
+    float prefill_ms;
+    float decode_ms;
+    uint32_t forward_steps;
+    uint32_t rows;
+} itts_gpt_timing;
+int itts_gpt_last_timing(const itts_gpt_ctx* ctx, itts_gpt_timing* out);
 
 /* ---- failure detection -------------------------------------------------------
  * Every device-side wait of the decode kernels (weight-ring slots, hand-off

@@ -2,3 +2,4 @@
 #define ITTS_WNS wf32
 #define ITTS_WBF16 0
 #include "decode_body.cuh"
+#include "decode_batch.cuh"

@@ -5,3 +5,4 @@
 #define ITTS_WNS wbf16
 #define ITTS_WBF16 1
 #include "decode_body.cuh"
+#include "decode_batch.cuh"

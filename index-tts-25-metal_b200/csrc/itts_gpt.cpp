@@ -23,11 +23,6 @@
 #include "mit2_bundle.hpp"
 #include "model.hpp"
 
-namespace itts {
-cudaError_t launch_beam_scores(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
-                               float beam_score, float* tmp, float* out, int* status, cudaStream_t s);
-}
-
 namespace {
 
 thread_local std::string g_create_error;
@@ -98,9 +93,7 @@ struct itts_gpt_ctx {
     size_t tagged_bytes = 0;        // bytes of the tagged hand-off region (db.qkv ...)
     uint32_t* d_hist = nullptr;     // processor history (grown on demand)
     size_t d_hist_cap = 0;
-    float* d_beam = nullptr;        // beam logits slots + scores
     void* d_sampler_big = nullptr;  // per-CTA sampler workspace
-    uint32_t beam_cap = 0;
     float* h_stage = nullptr;       // pinned [1024 * 1280]
     float* h_logits = nullptr;      // pinned [8194 * 10]
     uint32_t* h_codes = nullptr;    // pinned [kCap]
@@ -109,6 +102,19 @@ struct itts_gpt_ctx {
     bool have_prefill = false;
     uint64_t launches = 0;
     unsigned long long wait_ns = 0;  // device wait limit of decode launches (0: the kernels' default)
+    // batched decode (allocated on first use): KV arenas, activations, state
+    float* d_bkv = nullptr;          // b_arenas KV arenas of arena_floats each
+    uint32_t b_arenas = 0;
+    size_t arena_floats = 0;
+    char* d_bact = nullptr;          // activations, partials, counters, state, sets, codes, beam buffers
+    void* d_bbig = nullptr;          // kMaxBatch sampler workspaces
+    itts::BatchArgs bargs{};         // pointers into d_bact (M, options and flags are set per call)
+    float* d_bscores = nullptr;      // beam search: [kMaxBatch][8194] scores
+    float* d_btmp = nullptr;         // beam search: [kMaxBatch][8448] log-softmax scratch
+    uint32_t* d_bhist = nullptr;     // beam search: [kMaxBatch][kCap + 2] histories
+    itts::BatchState* h_bstate = nullptr;  // pinned
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // generate timing: start, prefill done, decode done
+    itts_gpt_timing timing{};        // accumulated over the last generate / generate_batch call
     bool pending = false;           // an async decode has not been synced yet
     uint32_t* pending_info = nullptr;
 
@@ -117,10 +123,12 @@ struct itts_gpt_ctx {
         if (stream) cudaStreamSynchronize(stream);
         for (void* p : {(void*)d_weights, (void*)d_model, (void*)d_kv, (void*)d_hidden, (void*)d_act,
                         (void*)d_history, (void*)d_codes, (void*)d_info, (void*)d_misc, (void*)d_hist,
-                        (void*)d_beam, d_sampler_big})
+                        d_sampler_big, (void*)d_bkv, (void*)d_bact, d_bbig})
             if (p) cudaFree(p);
-        for (void* p : {(void*)h_stage, (void*)h_logits, (void*)h_codes, (void*)h_ctl})
+        for (void* p : {(void*)h_stage, (void*)h_logits, (void*)h_codes, (void*)h_ctl, (void*)h_bstate})
             if (p) cudaFreeHost(p);
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -500,10 +508,182 @@ void apply_restore(itts_gpt_ctx* c, const itts_gpt_state* s) {
     c->cached = s->tokens;
 }
 
+// ------------------------------------------------------------ batched decode
+// Buffers of the batched path, allocated on first use; `arenas` KV arenas.
+void ensure_batch(itts_gpt_ctx* c, uint32_t arenas) {
+    using namespace itts;
+    if (!c->d_bact) {
+        const size_t B = kMaxBatch;
+        const size_t sizes[] = {B * kW * 4,                  // x
+                                B * 3840 * 4,                // qkv
+                                B * kW * 4,                  // attn
+                                B * kW * 4,                  // hm
+                                B * 5120 * 4,                // f
+                                B * kBatchLogitsStride * 4,  // logits
+                                B * kH * 8 * 68 * 4,         // attention partials
+                                size_t(24) * B * kH * 4,     // attention arrival counters
+                                sizeof(BatchState),          // step state
+                                B * kSeenWords * 4,          // repetition-penalty sets
+                                B * kCap * 4,                // codes
+                                B * kVocab * 4,              // beam scores
+                                B * 8448 * 4,                // beam log-softmax scratch
+                                B * (kCap + 2) * 4};         // beam histories
+        constexpr int n = int(sizeof(sizes) / sizeof(sizes[0]));
+        size_t total = 0;
+        for (size_t z : sizes) total += align256(z);
+        c->d_bact = dev_alloc<char>(total, "batched decode buffers");
+        ck(cudaMemset(c->d_bact, 0, total), "batched buffer init");
+        char* r[n];
+        char* p = c->d_bact;
+        for (int i = 0; i < n; ++i) {
+            r[i] = p;
+            p += align256(sizes[i]);
+        }
+        BatchArgs& a = c->bargs;
+        a.x = reinterpret_cast<float*>(r[0]);
+        a.qkv = reinterpret_cast<float*>(r[1]);
+        a.attn = reinterpret_cast<float*>(r[2]);
+        a.hm = reinterpret_cast<float*>(r[3]);
+        a.f = reinterpret_cast<float*>(r[4]);
+        a.logits = reinterpret_cast<float*>(r[5]);
+        a.part = reinterpret_cast<float*>(r[6]);
+        a.head_cnt = reinterpret_cast<unsigned*>(r[7]);
+        a.st = reinterpret_cast<BatchState*>(r[8]);
+        a.seen = reinterpret_cast<uint32_t*>(r[9]);
+        a.codes = reinterpret_cast<uint32_t*>(r[10]);
+        c->d_bscores = reinterpret_cast<float*>(r[11]);
+        c->d_btmp = reinterpret_cast<float*>(r[12]);
+        c->d_bhist = reinterpret_cast<uint32_t*>(r[13]);
+        c->d_bbig = dev_alloc<char>(B * sampler_big_bytes(), "batched sampler workspace");
+        a.big = reinterpret_cast<SamplerBig*>(c->d_bbig);
+        ck(cudaMallocHost(&c->h_bstate, sizeof(BatchState)), "pinned batch state");
+        c->arena_floats = size_t(c->layers) * 2 * kH * kCap * kHd;
+    }
+    if (c->b_arenas < arenas) {
+        if (c->d_bkv) cudaFree(c->d_bkv);
+        c->d_bkv = nullptr;
+        c->b_arenas = 0;
+        c->d_bkv = dev_alloc<float>(size_t(arenas) * c->arena_floats, "batched KV arenas");
+        c->b_arenas = arenas;
+    }
+    c->bargs.kv = c->d_bkv;
+    c->bargs.arena_floats = c->arena_floats;
+}
+
+// Batch arguments for M rows (options per row; scaled_head in the generate loop).
+itts::BatchArgs batch_args(itts_gpt_ctx* c, uint32_t M, const itts::SampleOpts* o, bool scaled_head) {
+    itts::BatchArgs a = c->bargs;
+    a.d = decode_args(c);
+    a.M = M;
+    for (uint32_t m = 0; m < M; ++m) a.opts[m] = o[m];
+    a.scaled_head = scaled_head ? 1 : 0;
+    return a;
+}
+
+// Prefill of one row into KV arena `arena`; its last-row logits go to row m
+// of the batched logits.
+void batch_prefill(itts_gpt_ctx* c, const float* prefix, size_t n_floats, uint32_t arena, uint32_t m) {
+    validate_prefix(n_floats);
+    if (!prefix) invalid("prefix is null");
+    const uint32_t rows = uint32_t(n_floats / kW);
+    ck(cudaMemcpyAsync(c->d_hidden, prefix, n_floats * 4, cudaMemcpyHostToDevice, c->stream), "prefix upload");
+    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x,    c->d_qkv,  c->d_att, c->d_r, c->d_ff,
+                        c->d_bkv + size_t(arena) * c->arena_floats, int(rows), c->dtype == ITTS_WEIGHTS_BF16,
+                        c->db.ctl->status};
+    ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
+    itts::DecodeArgs a = decode_args(c);
+    a.head_src = c->d_hidden + size_t(rows - 1) * kW;
+    a.b.logits = c->bargs.logits + size_t(m) * itts::kBatchLogitsStride;
+    ck(c->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_head(a, c->sm_count, c->stream)
+                                     : itts::wf32::launch_head(a, c->sm_count, c->stream),
+       "head launch");
+    ++c->launches;
+}
+
+void batch_forward(itts_gpt_ctx* c, const itts::BatchArgs& a) {
+    ck(c->dtype == ITTS_WEIGHTS_BF16
+           ? itts::wbf16::launch_batch_forward(a, int(c->layers), c->sm_count, c->stream, &c->launches)
+           : itts::wf32::launch_batch_forward(a, int(c->layers), c->sm_count, c->stream, &c->launches),
+       "batched forward launch");
+}
+
+// Device-time marks of a generate call (events on the context's stream):
+// 0 before the prefill(s), 1 before the token loop, 2 after it.
+void mark(itts_gpt_ctx* c, int k) { ck(cudaEventRecord(c->ev[k], c->stream), "event record"); }
+
+// After the call's final synchronisation: adds the marked intervals.
+void add_timing(itts_gpt_ctx* c, uint32_t forward_steps, uint32_t rows) {
+    float a = 0.f, b = 0.f;
+    ck(cudaEventElapsedTime(&a, c->ev[0], c->ev[1]), "event time");
+    ck(cudaEventElapsedTime(&b, c->ev[1], c->ev[2]), "event time");
+    c->timing.prefill_ms += a;
+    c->timing.decode_ms += b;
+    c->timing.forward_steps += forward_steps;
+    c->timing.rows = std::max(c->timing.rows, rows);
+}
+
+void put_state(itts_gpt_ctx* c) {
+    ck(cudaMemcpyAsync(c->bargs.st, c->h_bstate, sizeof(itts::BatchState), cudaMemcpyHostToDevice, c->stream),
+       "batch state upload");
+}
+
+// generate (gpt_sampling.cpp:168-189) for up to kMaxBatch greedy/sampled
+// requests in lockstep: each request is prefilled into its own KV arena, then
+// every step runs the sampler of every row and one batched forward step; a
+// row that stops is left out of later draws.
+void generate_rows(itts_gpt_ctx* c, size_t M, const float* const* prefixes, const size_t* n_floats,
+                   const itts::SampleOpts* o, uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes, int* stopped) {
+    using namespace itts;
+    ensure_batch(c, uint32_t(M));
+    reset_ctl(c);
+    ck(cudaMemsetAsync(c->bargs.head_cnt, 0, size_t(24) * kMaxBatch * kH * 4, c->stream), "counter reset");
+    mark(c, 0);
+    for (size_t m = 0; m < M; ++m) batch_prefill(c, prefixes[m], n_floats[m], uint32_t(m), uint32_t(m));
+    BatchState& st = *c->h_bstate;
+    std::memset(&st, 0, sizeof st);
+    std::vector<uint32_t> seen(size_t(M) * kSeenWords, 0u);
+    for (size_t m = 0; m < M; ++m) {
+        st.s0[m] = uint32_t(n_floats[m] / kW);
+        st.arena[m] = uint32_t(m);
+        for (uint32_t t : {1u, 8192u}) seen[m * kSeenWords + (t >> 5)] |= 1u << (t & 31);
+    }
+    st.active = (1u << M) - 1;
+    put_state(c);
+    ck(cudaMemcpyAsync(c->bargs.seen, seen.data(), seen.size() * 4, cudaMemcpyHostToDevice, c->stream), "seen upload");
+    BatchArgs a = batch_args(c, uint32_t(M), o, true);
+    a.max_codes = max_tokens;
+    mark(c, 1);
+    for (uint32_t i = 0; i < max_tokens; ++i) {
+        ck(launch_batch_sample(a, c->stream), "batched sampler launch");
+        ++c->launches;
+        if (i + 1 == max_tokens) break;
+        batch_forward(c, a);
+    }
+    mark(c, 2);
+    std::vector<uint32_t> out(size_t(M) * max_tokens);
+    ck(cudaMemcpyAsync(out.data(), c->bargs.codes, out.size() * 4, cudaMemcpyDeviceToHost, c->stream), "codes read");
+    ck(cudaMemcpyAsync(c->h_bstate, c->bargs.st, sizeof(BatchState), cudaMemcpyDeviceToHost, c->stream),
+       "batch state read");
+    check_status(c);
+    add_timing(c, max_tokens - 1, uint32_t(M));
+    for (size_t m = 0; m < M; ++m) {
+        n_codes[m] = st.n_codes[m];
+        stopped[m] = int(st.stopped[m]);
+        std::memcpy(codes + m * size_t(max_tokens), out.data() + m * size_t(max_tokens), size_t(st.n_codes[m]) * 4);
+    }
+    c->cached = 0;  // the context's own cache no longer follows a prefill
+    c->have_prefill = false;
+}
+
 // ------------------------------------------------------------ beam search
-// gpt_sampling.cpp:190-245.  The per-parent log-softmax, processors and beam
-// score run on the device (launch_beam_scores); candidate selection and the
-// hypothesis bookkeeping are the reference's host logic.
+// gpt_sampling.cpp:190-245 with the hypotheses decoded as the rows of one
+// batched step.  Each hypothesis owns a KV arena; a child keeps its parent's
+// arena when it is the parent's first surviving child, otherwise it takes an
+// arena no child claimed and the parent's cached rows are copied there on
+// the device.  Per step: the beam scores of every parent (float log-softmax,
+// processors with num_beams > 1 semantics, + the cumulative score) on the
+// device, the candidate choice and hypothesis bookkeeping of the reference on
+// the host, then one batched forward step of the children.
 uint64_t splitmix_draw(uint64_t seed, uint64_t n) {
     uint64_t z = seed + (n + 1) * 0x9E3779B97F4A7C15ULL;
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
@@ -553,23 +733,15 @@ uint32_t sample_flat(const std::vector<float>& s, int rng, uint64_t seed, uint64
 
 std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n_floats, const itts::SampleOpts& o,
                                   float length_penalty, uint32_t maximum, bool& eos_out) {
+    using namespace itts;
     const uint32_t nb = o.num_beams;
-    // slots: 2 * nb logits buffers + scratch + nb * 8194 scores
-    const uint32_t need = (2 * nb + 1 + nb) * 8448;
-    if (c->beam_cap < need) {
-        if (c->d_beam) cudaFree(c->d_beam);
-        c->d_beam = nullptr;
-        c->d_beam = dev_alloc<float>(need, "beam buffers");
-        c->beam_cap = need;
-    }
-    float* slots = c->d_beam;
-    float* tmp = slots + size_t(2 * nb) * 8448;
-    float* scores = tmp + 8448;
+    ensure_batch(c, nb);
+    reset_ctl(c);
+    ck(cudaMemsetAsync(c->bargs.head_cnt, 0, size_t(24) * kMaxBatch * kH * 4, c->stream), "counter reset");
     struct Beam {
         std::vector<uint32_t> codes;
         float score = 0;
-        int slot = -1;
-        std::shared_ptr<itts_gpt_state> state;
+        uint32_t arena = 0;
     };
     struct Finished {
         std::vector<uint32_t> codes;
@@ -580,44 +752,50 @@ std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n
         uint32_t parent, token;
         float score;
     };
+    const uint32_t rows = uint32_t(n_floats / kW);
+    mark(c, 0);
+    batch_prefill(c, prefix, n_floats, 0, 0);
+    // every initial hypothesis starts from the prefill's logits and arena 0 (gpt_sampling.cpp:196-198)
+    for (uint32_t p = 1; p < nb; ++p)
+        ck(cudaMemcpyAsync(c->bargs.logits + size_t(p) * kBatchLogitsStride, c->bargs.logits, kVocab * 4,
+                           cudaMemcpyDeviceToDevice, c->stream),
+           "beam logits");
+    std::vector<Beam> beams(nb);
+    for (uint32_t i = 1; i < nb; ++i) beams[i].score = -1e9f;
     uint64_t draws = 0;
     std::vector<Finished> finished;
-    host_prefill(c, prefix, n_floats);
-    ck(cudaMemcpyAsync(slots, c->db.logits, kVocab * 4, cudaMemcpyDeviceToDevice, c->stream), "beam logits");
-    Beam init;
-    init.slot = 0;
-    init.state.reset(make_checkpoint(c));
-    std::vector<Beam> beams(nb, init);
-    for (uint32_t i = 1; i < beams.size(); ++i) beams[i].score = -1e9f;
     auto finish = [&](const Beam& beam, float score, uint32_t length, bool eos) {
         finished.push_back({beam.codes, score / std::pow(static_cast<double>(std::max(length, 1u)), length_penalty), eos});
         std::sort(finished.begin(), finished.end(), [](const Finished& a, const Finished& b) { return a.score > b.score; });
         if (finished.size() > nb) finished.resize(nb);
     };
-    std::vector<uint32_t> hist;
+    const size_t hstride = kCap + 2;
+    std::vector<uint32_t> hist(hstride * nb);
     std::vector<float> all;
+    std::vector<SampleOpts> ro(nb, o);
+    uint32_t forwards = 0;
+    mark(c, 1);
     for (uint32_t si = 0; si < maximum; ++si) {
-        reset_ctl(c);
-        for (uint32_t p = 0; p < beams.size(); ++p) {
-            hist.assign({1u, 8192u});
-            hist.insert(hist.end(), beams[p].codes.begin(), beams[p].codes.end());
-            if (c->d_hist_cap < hist.size()) {
-                if (c->d_hist) cudaFree(c->d_hist);
-                c->d_hist = nullptr;
-                c->d_hist_cap = std::max<size_t>(hist.size(), 4096);
-                c->d_hist = dev_alloc<uint32_t>(c->d_hist_cap * (nb + 1), "history buffer");
-            }
-            uint32_t* dh = c->d_hist + size_t(p) * c->d_hist_cap;
-            ck(cudaMemcpyAsync(dh, hist.data(), hist.size() * 4, cudaMemcpyHostToDevice, c->stream), "history upload");
-            ck(itts::launch_beam_scores(slots + size_t(beams[p].slot) * 8448, o, dh, uint32_t(hist.size()),
-                                        beams[p].score, tmp, scores + size_t(p) * kVocab, c->db.ctl->status, c->stream),
+        const uint32_t np = uint32_t(beams.size());
+        for (uint32_t p = 0; p < np; ++p) {
+            uint32_t* h = hist.data() + p * hstride;
+            h[0] = 1;
+            h[1] = 8192;
+            std::copy(beams[p].codes.begin(), beams[p].codes.end(), h + 2);
+        }
+        ck(cudaMemcpyAsync(c->d_bhist, hist.data(), size_t(np) * hstride * 4, cudaMemcpyHostToDevice, c->stream),
+           "history upload");
+        for (uint32_t p = 0; p < np; ++p) {
+            ck(launch_beam_scores(c->bargs.logits + size_t(p) * kBatchLogitsStride, o, c->d_bhist + p * hstride,
+                                  uint32_t(beams[p].codes.size() + 2), beams[p].score, c->d_btmp + size_t(p) * 8448,
+                                  c->d_bscores + size_t(p) * kVocab, c->db.ctl->status, c->stream),
                "beam score launch");
             ++c->launches;
-            ck(cudaStreamSynchronize(c->stream), "beam score");  // hist staging is reused per parent
         }
-        all.resize(size_t(beams.size()) * kVocab);
-        ck(cudaMemcpyAsync(all.data(), scores, all.size() * 4, cudaMemcpyDeviceToHost, c->stream), "beam scores read");
-        check_status(c);
+        all.resize(size_t(np) * kVocab);
+        ck(cudaMemcpyAsync(all.data(), c->d_bscores, all.size() * 4, cudaMemcpyDeviceToHost, c->stream),
+           "beam scores read");
+        check_status(c);  // synchronises: the host buffers above are free again
         std::vector<Cand> cands;
         const uint32_t take = 2 * nb;
         if (o.do_sample) {
@@ -637,7 +815,7 @@ std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n
         }
         std::sort(cands.begin(), cands.end(), [](const Cand& a, const Cand& b) { return a.score > b.score; });
         std::vector<Beam> next;
-        const int slot_base = int((si + 1) % 2) * int(nb);
+        std::vector<uint32_t> parent_of;
         for (uint32_t rank = 0; rank < cands.size(); ++rank) {
             const Cand cand = cands[rank];
             const Beam& parent = beams[cand.parent];
@@ -650,19 +828,50 @@ std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n
             child.codes = parent.codes;
             child.codes.push_back(cand.token);
             child.score = cand.score;
-            if (si + 1 < maximum) {
-                apply_restore(c, parent.state.get());
-                device_step(c, cand.token, si + 2);
-                child.slot = slot_base + int(next.size());
-                ck(cudaMemcpyAsync(slots + size_t(child.slot) * 8448, c->db.logits, kVocab * 4,
-                                   cudaMemcpyDeviceToDevice, c->stream),
-                   "beam logits");
-                child.state.reset(make_checkpoint(c));
-            }
             next.push_back(std::move(child));
+            parent_of.push_back(cand.parent);
             if (next.size() == nb) break;
         }
         if (next.empty()) break;
+        if (si + 1 < maximum) {
+            // a parent's first child keeps its arena; later children get a copy
+            std::vector<char> claimed(nb, 0);
+            std::vector<int> src(next.size(), -1);
+            for (size_t i = 0; i < next.size(); ++i) {
+                const uint32_t pa = beams[parent_of[i]].arena;
+                if (!claimed[pa]) {
+                    claimed[pa] = 1;
+                    next[i].arena = pa;
+                } else {
+                    src[i] = int(pa);
+                }
+            }
+            const size_t width = size_t(rows + si) * kHd * 4;  // the parent's cached rows
+            for (size_t i = 0; i < next.size(); ++i) {
+                if (src[i] < 0) continue;
+                uint32_t dst = 0;
+                while (claimed[dst]) ++dst;
+                claimed[dst] = 1;
+                next[i].arena = dst;
+                const float* from = c->d_bkv + size_t(src[i]) * c->arena_floats;
+                float* to = c->d_bkv + size_t(dst) * c->arena_floats;
+                ck(cudaMemcpy2DAsync(to, size_t(kCap) * kHd * 4, from, size_t(kCap) * kHd * 4, width,
+                                     size_t(c->layers) * 2 * kH, cudaMemcpyDeviceToDevice, c->stream),
+                   "beam KV copy");
+            }
+            BatchState& st = *c->h_bstate;
+            std::memset(&st, 0, sizeof st);
+            for (size_t i = 0; i < next.size(); ++i) {
+                st.token[i] = next[i].codes.back();
+                st.s0[i] = rows;
+                st.arena[i] = next[i].arena;
+            }
+            st.active = (1u << next.size()) - 1;
+            st.step = si + 1;  // forward step si: mel position si + 2 over rows + si cached tokens
+            put_state(c);
+            batch_forward(c, batch_args(c, uint32_t(next.size()), ro.data(), false));
+            ++forwards;
+        }
         beams = std::move(next);
         if (finished.size() == nb &&
             finished.back().score >= cands[0].score / std::pow(static_cast<double>(si + 1), length_penalty)) {
@@ -670,10 +879,14 @@ std::vector<uint32_t> beam_search(itts_gpt_ctx* c, const float* prefix, size_t n
             break;
         }
     }
+    mark(c, 2);
     check_status(c);
+    add_timing(c, forwards, nb);
     for (const auto& beam : beams) finish(beam, beam.score, uint32_t(beam.codes.size()), false);
     if (finished.empty()) fail(ITTS_ERR_RUNTIME, "Beam search produced no hypotheses");
     eos_out = finished[0].eos;
+    c->cached = 0;  // the context's own cache no longer follows a prefill
+    c->have_prefill = false;
     return finished[0].codes;
 }
 
@@ -734,8 +947,11 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
         ck(weight_dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::decode_configure(&per_sm)
                                              : itts::wf32::decode_configure(&per_sm),
            "decode kernel configuration");
+        ck(weight_dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::batch_configure() : itts::wf32::batch_configure(),
+           "batched kernel configuration");
         if (per_sm < 1) fail(ITTS_ERR_RUNTIME, "persistent decode kernel does not fit on an SM");
         ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream creation");
+        for (cudaEvent_t& e : c->ev) ck(cudaEventCreate(&e), "event creation");
         upload_weights(c.get(), bundle);
         alloc_buffers(c.get());
         ck(cudaDeviceSynchronize(), "load");
@@ -834,6 +1050,7 @@ void generate_one(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const
         *stopped = eos ? 1 : 0;
         return;
     }
+    mark(ctx, 0);
     host_prefill(ctx, prefix, n_floats);
     itts::DecodeArgs a = decode_args(ctx);
     a.mode = itts::kModeGenerate;
@@ -841,11 +1058,14 @@ void generate_one(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, const
     a.s0 = ctx->cached;
     a.pos0 = 2;  // first generated code sits at mel position 2 (gpt_sampling.cpp:184-186)
     a.opts = o;
+    mark(ctx, 1);
     launch_decode(ctx, a);
+    mark(ctx, 2);
     ck(cudaMemcpyAsync(ctx->h_codes, ctx->d_codes, size_t(max_tokens) * 4, cudaMemcpyDeviceToHost, ctx->stream),
        "codes read");
     check_status(ctx);
     const itts::DecodeCtl& ctl = *ctx->h_ctl;
+    add_timing(ctx, ctl.info[3], 1);
     ctx->cached += ctl.info[3];
     *n_codes = ctl.info[0];
     *stopped = int(ctl.info[1]);
@@ -861,6 +1081,7 @@ int itts_gpt_generate(itts_gpt_ctx* ctx, const float* prefix, size_t n_floats, c
         validate_capacity(ctx, n_floats / kW, max_tokens);
         float lp = 0;
         const itts::SampleOpts o = configure(*opts, &lp);
+        ctx->timing = itts_gpt_timing{};
         generate_one(ctx, prefix, n_floats, o, lp, max_tokens, codes, n_codes, stopped);
     });
 }
@@ -880,9 +1101,43 @@ int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const*
             validate_capacity(ctx, n_floats[i] / kW, max_tokens);
             o[i] = configure(opts[i], &lp[i]);
         }
-        for (size_t i = 0; i < batch; ++i)
+        ctx->timing = itts_gpt_timing{};
+        // beam requests run one at a time; the others decode in lockstep,
+        // up to kMaxBatch rows per batched launch sequence
+        std::vector<size_t> rows;
+        for (size_t i = 0; i < batch; ++i) {
+            if (o[i].num_beams > 1)
+                generate_one(ctx, prefixes[i], n_floats[i], o[i], lp[i], max_tokens, codes + i * size_t(max_tokens),
+                             n_codes + i, stopped + i);
+            else
+                rows.push_back(i);
+        }
+        if (rows.size() == 1) {
+            const size_t i = rows[0];
             generate_one(ctx, prefixes[i], n_floats[i], o[i], lp[i], max_tokens, codes + i * size_t(max_tokens),
                          n_codes + i, stopped + i);
+            return;
+        }
+        for (size_t b0 = 0; b0 < rows.size(); b0 += itts::kMaxBatch) {
+            const size_t M = std::min<size_t>(itts::kMaxBatch, rows.size() - b0);
+            std::vector<const float*> pp(M);
+            std::vector<size_t> nf(M);
+            std::vector<itts::SampleOpts> oo(M);
+            std::vector<uint32_t> cc(M * size_t(max_tokens)), nc(M);
+            std::vector<int> sp(M);
+            for (size_t k = 0; k < M; ++k) {
+                pp[k] = prefixes[rows[b0 + k]];
+                nf[k] = n_floats[rows[b0 + k]];
+                oo[k] = o[rows[b0 + k]];
+            }
+            generate_rows(ctx, M, pp.data(), nf.data(), oo.data(), max_tokens, cc.data(), nc.data(), sp.data());
+            for (size_t k = 0; k < M; ++k) {
+                const size_t i = rows[b0 + k];
+                n_codes[i] = nc[k];
+                stopped[i] = sp[k];
+                std::memcpy(codes + i * size_t(max_tokens), cc.data() + k * size_t(max_tokens), size_t(nc[k]) * 4);
+            }
+        }
     });
 }
 
@@ -1012,6 +1267,12 @@ int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode) {
 }
 
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int itts_gpt_last_timing(const itts_gpt_ctx* ctx, itts_gpt_timing* out) {
+    if (!ctx || !out) return ITTS_ERR_INVALID_ARGUMENT;
+    *out = ctx->timing;
+    return ITTS_OK;
+}
 
 int itts_gpt_set_wait_limit(itts_gpt_ctx* ctx, uint64_t ns) {
     if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;

@@ -103,6 +103,52 @@ struct DecodeArgs {
     unsigned long long wait_ns;  // time limit of every device-side wait; 0: the default (2 s)
 };
 
+// ---- batched decode (M rows per step) ------------------------------------
+// Up to kMaxBatch independent rows (requests or beam hypotheses) advance one
+// token per step together; each weight byte is read once per step for all
+// rows.  Per-row arithmetic is that of the batch-1 kernels, so every row's
+// logits are bit-identical to a batch-1 decode of the same row.
+constexpr int kMaxBatch = 16;
+
+// Device-resident per-step state of a batched decode (read by every kernel of
+// a step, advanced by the sampler kernel), so one launch sequence serves every
+// step.
+struct BatchState {
+    uint32_t token[kMaxBatch];    // code each row feeds to the next forward step
+    uint32_t s0[kMaxBatch];       // cached tokens of the row before forward step 0
+    uint32_t arena[kMaxBatch];    // KV arena of the row
+    uint32_t n_codes[kMaxBatch];  // codes generated so far
+    uint32_t stopped[kMaxBatch];  // 1 when the stop code ended the row
+    uint32_t active;              // bit m: row m still decodes
+    uint32_t step;                // index of the next draw; forward step step-1 feeds token[]
+    uint32_t sample_arrivals;     // sampler CTAs that finished the current draw
+    uint32_t pad[5];
+};
+
+struct BatchArgs {
+    DecodeArgs d;      // weight table, status word, wait limit (ring and waits of the shared code)
+    uint32_t M;        // rows (1..kMaxBatch)
+    float* x;          // [kMaxBatch][1280] residual stream entering / leaving a layer
+    float* qkv;        // [kMaxBatch][3840]
+    float* attn;       // [kMaxBatch][1280]
+    float* hm;         // [kMaxBatch][1280]
+    float* f;          // [kMaxBatch][5120]
+    float* logits;     // [kMaxBatch][8448]
+    float* part;       // [kMaxBatch][20][8][68] split-K attention partials
+    unsigned* head_cnt;  // [24][kMaxBatch][20] attention arrivals (the last arriver resets)
+    float* kv;         // arena 0; arena a starts at kv + a * arena_floats
+    size_t arena_floats;
+    BatchState* st;
+    uint32_t* codes;   // generate: [kMaxBatch][max_codes]
+    uint32_t max_codes;
+    uint32_t* seen;    // [kMaxBatch][257] repetition-penalty sets
+    SamplerBig* big;   // [kMaxBatch] sampler workspaces
+    SampleOpts opts[kMaxBatch];
+    int scaled_head;   // head applies repetition penalty and temperature (generate loop)
+};
+constexpr size_t kBatchLogitsStride = 8448;
+constexpr int kSeenWords = 257;  // ceil(8194 / 32)
+
 // ---- host-side launchers ----------------------------------------------------
 // decode_body.cuh, once per weight type: wf32 (decode.cu), wbf16 (decode_bf16.cu)
 #define ITTS_DECLARE_DECODE_LAUNCHERS(NS)                                                                      \
@@ -114,6 +160,9 @@ struct DecodeArgs {
                                       uint64_t* launches);                                                     \
     cudaError_t launch_head(const DecodeArgs& a, int ncta, cudaStream_t s);                                    \
     cudaError_t launch_wait_probe(const DecodeArgs& a, int ncta, cudaStream_t s);                              \
+    cudaError_t batch_configure();                                                                             \
+    cudaError_t launch_batch_forward(const BatchArgs& a, int layers, int ncta, cudaStream_t s,                 \
+                                     uint64_t* launches);                                                      \
     }
 ITTS_DECLARE_DECODE_LAUNCHERS(wf32)
 ITTS_DECLARE_DECODE_LAUNCHERS(wbf16)
@@ -127,6 +176,9 @@ cudaError_t launch_layer_sample(const DecodeArgs& a, uint32_t i, cudaStream_t s)
 cudaError_t launch_layer_finish(const DecodeArgs& a, cudaStream_t s);
 cudaError_t launch_processors(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
                               float* out, int* status, cudaStream_t s);
+cudaError_t launch_batch_sample(const BatchArgs& a, cudaStream_t s);
+cudaError_t launch_beam_scores(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
+                               float beam_score, float* tmp, float* out, int* status, cudaStream_t s);
 
 struct PrefillArgs {
     const ModelW* hw;  // host copy (pointers to device memory)

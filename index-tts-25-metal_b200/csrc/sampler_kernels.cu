@@ -92,12 +92,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_beam_scores(const float* logits
         mx = fmaxf(mx, v[k]);
     }
     const float peak = block_max(mx, sm.redf);
-    float s = 0.f;
+    // The reference sums std::exp(v - peak) in float, one term after another
+    // in index order, then adds std::log(sum) to the peak.  Each exp and the
+    // log are rounded once from double (correctly rounded up to rare ties,
+    // where the host's libm may round differently) and one thread adds the
+    // terms in index order.
+    float* terms = big->sv_s;  // the sampler's workspace is free until run_sampler
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
-        if (k < cnt) s += expf(v[k] - peak);
-    const float sum = block_sum(s, sm.redf);
-    const float log_sum = peak + logf(sum);
+        if (k < cnt) terms[base + k] = (float)exp((double)(v[k] - peak));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float sum = 0.f;
+        for (int i = 0; i < kVocab; ++i) sum += terms[i];
+        sm.redf[0] = peak + (float)log((double)sum);
+    }
+    __syncthreads();
+    const float log_sum = sm.redf[0];
+    __syncthreads();  // sm.redf is reused by the sampler below
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
         if (k < cnt) tmp[base + k] = v[k] - log_sum;
@@ -110,12 +122,62 @@ __global__ void __launch_bounds__(kThreads, 1) k_beam_scores(const float* logits
         if (k < cnt) out[base + k] = out[base + k] + beam_score;
 }
 
+// Batched generate loop, draw st->step of every active row (one CTA per row):
+// the processors and the token choice of the batch-1 loop (k_decode's
+// sample_next) on the row's logits, then the row's bookkeeping -- code,
+// count, stop (gpt_sampling.cpp:178-187) and repetition-penalty set.  The last
+// CTA to finish advances st->step.
+__global__ void __launch_bounds__(kThreads, 1) k_batch_sample(BatchArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(smem_raw);
+    SamplerBig* big = reinterpret_cast<SamplerBig*>(smem_raw + kSamplerSmallBytes);
+    BatchState* st = a.st;
+    const uint32_t m = blockIdx.x;
+    const uint32_t i = (uint32_t)ld_volatile((const int*)&st->step);
+    const bool active = (ld_volatile((const int*)&st->active) >> m) & 1;
+    int* status = a.d.b.ctl->status;
+    if (active) {
+        uint32_t* seen = a.seen + (size_t)m * kSeenWords;
+        for (int k = threadIdx.x; k < kBits; k += kThreads) sm.seen[k] = seen[k];
+        __syncthreads();
+        const SampleOpts& o = a.opts[m];
+        // draw 0 reads the prefill's raw logits; later draws read the head's scaled scores
+        const uint32_t token = run_sampler(a.logits + (size_t)m * kBatchLogitsStride, o, i, o.do_sample == 0, sm, big,
+                                           nullptr, status, a.scaled_head && i > 0);
+        if (threadIdx.x == 0) {
+            const uint32_t bit = 1u << m;
+            if (token == (uint32_t)kStopCode) {
+                st->stopped[m] = 1;
+                atomicAnd(&st->active, ~bit);
+            } else if (token >= (uint32_t)kStartCode) {
+                if (token != 0xffffffffu) set_status(status, kStatusInvalidCode, 300, (int)token);
+                atomicAnd(&st->active, ~bit);
+            } else {
+                a.codes[(size_t)m * a.max_codes + i] = token;
+                st->n_codes[m] = i + 1;
+                st->token[m] = token;
+                atomicOr(&seen[token >> 5], 1u << (token & 31));
+                if (i + 1 == a.max_codes) atomicAnd(&st->active, ~bit);
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t old = atomicAdd(&st->sample_arrivals, 1u);
+        if (old == a.M - 1) {
+            st->sample_arrivals = 0;
+            st->step = i + 1;
+        }
+    }
+}
+
 // ------------------------------------------------------------ host side
 size_t sampler_big_bytes() { return sizeof(SamplerBig); }
 size_t sampler_dyn_smem_bytes() { return kSamplerDynSmem; }
 
 cudaError_t sampler_configure() {
-    for (const void* f : {(const void*)k_layer_sample, (const void*)k_processors, (const void*)k_beam_scores}) {
+    for (const void* f : {(const void*)k_layer_sample, (const void*)k_processors, (const void*)k_beam_scores,
+                          (const void*)k_batch_sample}) {
         const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSamplerDynSmem);
         if (e != cudaSuccess) return e;
     }
@@ -129,6 +191,11 @@ cudaError_t launch_layer_sample(const DecodeArgs& a, uint32_t i, cudaStream_t s)
 
 cudaError_t launch_layer_finish(const DecodeArgs& a, cudaStream_t s) {
     k_layer_finish<<<1, 1, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_batch_sample(const BatchArgs& a, cudaStream_t s) {
+    k_batch_sample<<<a.M, kThreads, kSamplerDynSmem, s>>>(a);
     return cudaGetLastError();
 }
 

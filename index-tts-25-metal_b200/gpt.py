@@ -45,6 +45,12 @@ class GenOpts(C.Structure):
                 ("length_penalty", C.c_float), ("rng", C.c_int32)]
 
 
+class Timing(C.Structure):
+    """itts_gpt_timing: device time of the last generate call."""
+    _fields_ = [("prefill_ms", C.c_float), ("decode_ms", C.c_float), ("forward_steps", C.c_uint32),
+                ("rows", C.c_uint32)]
+
+
 class Info(C.Structure):
     _fields_ = [("layers", C.c_uint32), ("mel_pos_rows", C.c_uint32), ("text_pos_rows", C.c_uint32),
                 ("sm_count", C.c_uint32), ("weight_bytes", C.c_uint64), ("stream_bytes", C.c_uint64),
@@ -85,6 +91,7 @@ SIGNATURES = {
     "itts_gpt_set_decode_mode": (C.c_int, [_P, C.c_int]),
     "itts_gpt_launch_count": (C.c_uint64, [_P]),
     "itts_gpt_set_wait_limit": (C.c_int, [_P, C.c_uint64]),
+    "itts_gpt_last_timing": (C.c_int, [_P, C.POINTER(Timing)]),
     "itts_gpt_wait_probe": (C.c_int, [_P]),
     "itts_gpt_apply_processors_noalloc": (C.c_int, [C.c_int, _P, C.c_size_t, _P, C.c_size_t, C.POINTER(GenOpts),
                                                     _P]),
@@ -214,6 +221,12 @@ class GptDecoder:
     @property
     def launch_count(self) -> int:
         return self._lib.itts_gpt_launch_count(self._h)
+
+    def last_timing(self) -> Timing:
+        """Device time (prefill, token loop) of the last generate call."""
+        t = Timing()
+        self._check(self._lib.itts_gpt_last_timing(self._h, C.byref(t)))
+        return t
 
     def set_wait_limit(self, ns: int):
         """Time limit of the decode kernels' device-side waits (0: default 2 s)."""
