@@ -5,18 +5,26 @@
 // is compiled once per weight type like the batch-1 kernels and shares their
 // weight ring, producer warp, segment schedule and LayerNorm merge.
 //
-// One forward step (src/gpt.cpp:88-125, initial=false, for M rows) is one
-// launch per phase, the launch boundary being the grid-wide hand-off:
+// One forward step (src/gpt.cpp:88-125, initial=false, for M rows) is five
+// phases per layer plus the head, each followed by a grid-wide hand-off:
 //   k_bgemv<QKV>   LN1 + c_attn rows            x    -> qkv  (and the L2
 //                                                             prefetch of the K/V)
 //   k_battn        split-K attention + K/V append qkv -> attn (kernels.metal:2064-2145)
 //   k_bgemv<OPROJ> attn.c_proj rows + residual  attn -> hm
 //   k_bgemv<FC>    LN2 + c_fc rows + GELU       hm   -> f
 //   k_bgemv<MP>    mlp.c_proj rows + residual   f    -> x
-// x 24 layers, then k_bgemv<HEAD> (ln_f -> final_norm -> mel_head) and the
-// sampler (sampler_kernels.cu, one CTA per row).  Per-step values (codes fed,
-// cached tokens, positions) live in device memory (BatchState), so the same
-// launch sequence serves every step.
+// x 24 layers, then the head (ln_f -> final_norm -> mel_head) and one
+// sampler per row.  Two drivers run the same phase code:
+//   * k_bdecode: one cooperative launch (one CTA per SM) for many steps; the
+//     producer warp streams the weights of step after step through the ring
+//     while the phases meet at grid barriers, and CTA m samples row m.
+//   * the layered kernels (one launch per phase, k_batch_sample for the
+//     draws): diagnostic and non-cooperative path.
+// Rows join and leave independently (continuous batching): a row's draw i
+// happens at global step base[m] + i and feeds forward step i (mel position
+// 2 + i, s0 + i cached tokens); rows that are not active are skipped by the
+// attention units and the epilogues.  Per-step values live in device memory
+// (BatchState).
 //
 // Same numbers as batch 1.  Every output of a row is computed with the
 // operations, operands and order of the batch-1 kernels:
@@ -60,16 +68,41 @@ struct BGeo {
     static_assert(RS >= 1 && RS * kWarpsPerRow == WPG && RPW * RS == kRowsPerSlot, "batch GEMV geometry");
 };
 
+// Split-K attention units of every active row (batch-1 chunking per row),
+// enumerated row-major.
+struct BUnits {
+    uint32_t start[kMaxBatch + 1];  // first unit of each row
+    uint32_t nch[kMaxBatch], ch[kMaxBatch], S[kMaxBatch];
+};
+
+// Attention scratch for P units at a time: the 16 virtual-warp states of
+// each unit, its q/k/v, its (row, head, chunk).
+template <int P>
+struct BAttnSmem {
+    float vm[P][kWarps], vl[P][kWarps];
+    float vo[P][kWarps][kHeadDim];
+    __align__(16) float qkvh[P][3 * kHeadDim];
+    uint32_t um[P], uh[P], uc[P];
+    int last[P];
+    BUnits units;
+};
+constexpr int kUnitsPersistent = 4;  // per pass in k_bdecode (shares shared memory with the ring)
+constexpr int kUnitsLayered = 8;     // per pass in k_battn
+
 struct BatchSmem {
     Ring ring;
     ModelW w;
     union {
         float red[kMaxRowsPerCta][kWarpsPerRow][kMaxBatch];  // 1280-wide rows: block sums (row, q, m)
         float longred[kLongRowsMax][kWarpsPerLong][kMaxBatch];
+        BAttnSmem<kUnitsPersistent> at;
+        SamplerSmem sa;
     };
     float wstat[kMPG][kWarps][2];
+    int abort;
 };
-static_assert(sizeof(BatchSmem) <= 227 * 1024, "batched GEMV shared memory above the sm_100 per-CTA limit");
+static_assert(sizeof(BatchSmem) <= 227 * 1024, "batched decode shared memory above the sm_100 per-CTA limit");
+
 
 struct BCtx {
     const BatchArgs& a;
@@ -90,12 +123,6 @@ __device__ __forceinline__ const wtype* bslot_wait(BCtx& cx, uint32_t k, bool& o
 __device__ __forceinline__ void bslot_release(BCtx& cx, uint32_t k) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(&cx.R.empty[k % kSlots]);
-}
-
-// The forward step whose inputs the current launch computes: its codes were
-// drawn as draw step-1 (mel position 2 + step - 1, S = s0 + step - 1).
-__device__ __forceinline__ uint32_t fwd_index(const BatchState* st) {
-    return (uint32_t)ld_volatile((const int*)&st->step) - 1u;
 }
 
 // Dot products of kMPG rows' inputs with one weight row: the two fma chains
@@ -241,6 +268,15 @@ __device__ void layernorm_rows(float2 (&x)[kMPG][kVec], const float2 (&g)[kVec],
         }
 }
 
+// ------------------------------------------------------------- rows
+__device__ __forceinline__ uint32_t rows_active(const BatchArgs& a) {
+    return (uint32_t)ld_volatile((const int*)&a.st->active);
+}
+// Forward step of row m whose input is the code drawn at global step gstep.
+__device__ __forceinline__ uint32_t row_fwd(const BatchArgs& a, uint32_t m, uint32_t gstep) {
+    return gstep - a.st->base[m];
+}
+
 // Batch row of this warp's input registers slot mm (its group's rows).
 template <int G>
 __device__ __forceinline__ int group_row(int mm) {
@@ -248,21 +284,26 @@ __device__ __forceinline__ int group_row(int mm) {
 }
 
 // Input vectors of this warp's rows at its GEMV columns: src + m * stride
-// (rows >= M read as zero).  At layer 0 the residual stream is the token
-// embedding (gpt_build_current, kernels.metal:1310-1325).
+// (inactive rows and rows >= M read as zero).  At layer 0 the residual stream
+// is the token embedding (gpt_build_current, kernels.metal:1310-1325).
 template <int G>
-__device__ __forceinline__ void load_rows(const BCtx& cx, const float* src, size_t stride, bool embed, uint32_t pos,
-                                          float2 (&x)[kMPG][kVec]) {
+__device__ __forceinline__ void load_rows(const BCtx& cx, const float* src, size_t stride, bool embed, uint32_t act,
+                                          uint32_t gstep, float2 (&x)[kMPG][kVec]) {
 #pragma unroll
     for (int mm = 0; mm < kMPG; ++mm) {
         const int m = group_row<G>(mm);
+        const bool on = m < (int)cx.a.M && ((act >> m) & 1u);
+        uint32_t tok = 0, pos = 0;
+        if (on && embed) {
+            tok = __ldcg(&cx.a.st->token[m]);
+            pos = 2 + row_fwd(cx.a, m, gstep);
+        }
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
             const int c = col_of(j);
-            if (m >= (int)cx.a.M) {
+            if (!on) {
                 x[mm][j] = make_float2(0.f, 0.f);
             } else if (embed) {
-                const uint32_t tok = cx.a.st->token[m];
                 const float2 e = __ldg(reinterpret_cast<const float2*>(cx.w.mel_emb + (size_t)tok * kWidth + c));
                 const float2 p = __ldg(reinterpret_cast<const float2*>(cx.w.mel_pos + (size_t)pos * kWidth + c));
                 x[mm][j] = make_float2(e.x + p.x, e.y + p.y);
@@ -273,10 +314,10 @@ __device__ __forceinline__ void load_rows(const BCtx& cx, const float* src, size
     }
 }
 
-// y[row][m] = W[row, :] . x_m for `nrows` streamed 1280-wide rows and the M
-// rows of the batch; epi(row, m, y) runs once all slots are consumed.
+// y[row][m] = W[row, :] . x_m for `nrows` streamed 1280-wide rows and the
+// active rows of the batch; epi(row, m, y) runs once all slots are consumed.
 template <int G, class Epi>
-__device__ bool bgemv_1280(BCtx& cx, int nrows, const float2 (&x)[kMPG][kVec], int where, Epi epi) {
+__device__ bool bgemv_1280(BCtx& cx, int nrows, const float2 (&x)[kMPG][kVec], uint32_t act, int where, Epi epi) {
     using Geo = BGeo<G>;
     const int warp = threadIdx.x >> 5;
     const int wg = warp % Geo::WPG, rs = wg / kWarpsPerRow, q = wg % kWarpsPerRow;
@@ -310,11 +351,13 @@ __device__ bool bgemv_1280(BCtx& cx, int nrows, const float2 (&x)[kMPG][kVec], i
     if (csync_or(!ok)) return false;
     for (int t = threadIdx.x; t < nrows * M; t += kThreads) {
         const int row = t / M, m = t % M;
+        if (!((act >> m) & 1u)) continue;
         float v = cx.sm.red[row][0][m];
 #pragma unroll
         for (int i = 1; i < kWarpsPerRow; ++i) v += cx.sm.red[row][i][m];
         epi(row, m, v);
     }
+    csync();  // red is reused (and shares memory with the attention and sampler scratch)
     return true;
 }
 
@@ -323,7 +366,7 @@ __device__ bool bgemv_1280(BCtx& cx, int nrows, const float2 (&x)[kMPG][kVec], i
 // (their inputs in registers, batch-1 column layout); the slots go back to
 // the producer after the last pass.
 template <int G, class Epi>
-__device__ bool bgemv_long(BCtx& cx, int nrows, int where, Epi epi) {
+__device__ bool bgemv_long(BCtx& cx, int nrows, uint32_t act, int where, Epi epi) {
     const int warp = threadIdx.x >> 5;
     const int rr = warp / kWarpsPerLong, q = warp % kWarpsPerLong;
     const int M = (int)cx.a.M;
@@ -331,15 +374,16 @@ __device__ bool bgemv_long(BCtx& cx, int nrows, int where, Epi epi) {
     bool ok = true;
 #pragma unroll 1
     for (int g = 0; g < G && ok; ++g) {
-        if (g * kMPG >= M) break;
+        if (g > 0 && ((act >> (g * kMPG)) & ((1u << kMPG) - 1u)) == 0) continue;  // no active row in the group
         float2 x[kMPG][kVec];
 #pragma unroll
         for (int mm = 0; mm < kMPG; ++mm) {
             const int m = g * kMPG + mm;
+            const bool on = m < M && ((act >> m) & 1u);
 #pragma unroll
             for (int j = 0; j < kVec; ++j)
-                x[mm][j] = m < M ? __ldcg(reinterpret_cast<const float2*>(cx.a.f + (size_t)m * kFfn + long_col_of(j)))
-                                 : make_float2(0.f, 0.f);
+                x[mm][j] = on ? __ldcg(reinterpret_cast<const float2*>(cx.a.f + (size_t)m * kFfn + long_col_of(j)))
+                              : make_float2(0.f, 0.f);
         }
 #pragma unroll 1
         for (int si = 0; si < nslots; ++si) {
@@ -371,6 +415,7 @@ __device__ bool bgemv_long(BCtx& cx, int nrows, int where, Epi epi) {
     if (csync_or(!ok)) return false;
     for (int t = threadIdx.x; t < nrows * M; t += kThreads) {
         const int row = t / M, m = t % M;
+        if (!((act >> m) & 1u)) continue;
         float v[kWarpsPerLong / 2];
 #pragma unroll
         for (int i = 0; i < kWarpsPerLong / 2; ++i) v[i] = cx.sm.longred[row][2 * i][m] + cx.sm.longred[row][2 * i + 1][m];
@@ -380,25 +425,22 @@ __device__ bool bgemv_long(BCtx& cx, int nrows, int where, Epi epi) {
             for (int i = 0; i < w; ++i) v[i] = v[2 * i] + v[2 * i + 1];
         epi(row, m, v[0]);
     }
+    csync();
     return true;
 }
 
 // --------------------------------------------------------------- attention
-// Split-K units of every row (batch-1 chunking per row), enumerated row-major.
-struct BUnits {
-    uint32_t start[kMaxBatch + 1];  // first unit of each row
-    uint32_t nch[kMaxBatch], ch[kMaxBatch], S[kMaxBatch];
-};
-
-__device__ __forceinline__ void batch_units(const BatchArgs& a, int ncta, uint32_t fwd, BUnits& u) {
+__device__ __forceinline__ void batch_units(const BatchArgs& a, int ncta, uint32_t act, uint32_t gstep, BUnits& u) {
     uint32_t acc = 0;
     for (uint32_t m = 0; m < a.M; ++m) {
-        const uint32_t S = a.st->s0[m] + fwd, keys = S + 1;
+        u.start[m] = acc;
+        u.nch[m] = u.ch[m] = u.S[m] = 0;
+        if (!((act >> m) & 1u)) continue;
+        const uint32_t S = a.st->s0[m] + row_fwd(a, m, gstep), keys = S + 1;
         const uint32_t ch = attn_chunk(keys, ncta);
         u.S[m] = S;
         u.ch[m] = ch;
         u.nch[m] = (keys + ch - 1) / ch;
-        u.start[m] = acc;
         acc += kHeads * u.nch[m];
     }
     u.start[a.M] = acc;
@@ -409,29 +451,19 @@ __device__ __forceinline__ float* arena_kv(const BatchArgs& a, uint32_t m, int l
            (((size_t)li * 2 + kv) * kHeads + h) * (size_t)kKvCapacity * kHeadDim;
 }
 
-constexpr int kUnitsPerPass = 8;
-
-struct BAttnSmem {
-    float vm[kUnitsPerPass][kWarps], vl[kUnitsPerPass][kWarps];
-    float vo[kUnitsPerPass][kWarps][kHeadDim];
-    __align__(16) float qkvh[kUnitsPerPass][3 * kHeadDim];
-    uint32_t um[kUnitsPerPass], uh[kUnitsPerPass], uc[kUnitsPerPass];
-    int last[kUnitsPerPass];
-    BUnits units;
-};
-
-__global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
-    __shared__ BAttnSmem sm;
-    if (ld_volatile((const int*)&a.st->active) == 0) return;
-    const int cta = blockIdx.x, ncta = gridDim.x;
+// Split-K attention of layer li for every active row, P units of this CTA at
+// a time (kernels.metal:2064-2145; batch-1 phase_attn per unit).  Called by
+// the kThreads consumer threads.
+template <int P>
+__device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t gstep, int cta, int ncta,
+                            BAttnSmem<P>& sm) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const uint32_t fwd = fwd_index(a.st);
-    if (t == 0) batch_units(a, ncta, fwd, sm.units);
-    __syncthreads();
+    if (t == 0) batch_units(a, ncta, act, gstep, sm.units);
+    csync();
     const uint32_t total = sm.units.start[a.M];
 #pragma unroll 1
-    for (uint32_t base = cta; base < total; base += (uint32_t)ncta * kUnitsPerPass) {
-        if (t < kUnitsPerPass) {
+    for (uint32_t base = cta; base < total; base += (uint32_t)ncta * P) {
+        if (t < P) {
             const uint32_t u = base + (uint32_t)t * ncta;
             if (u < total) {
                 uint32_t m = 0;
@@ -444,20 +476,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
                 sm.um[t] = 0xffffffffu;
             }
         }
-        __syncthreads();
-        int P = 0;
-        for (int i = 0; i < kUnitsPerPass; ++i) P += sm.um[i] != 0xffffffffu;
+        csync();
+        int np = 0;
+        for (int i = 0; i < P; ++i) np += sm.um[i] != 0xffffffffu;
         // q, k, v of each unit's head: 3 x 16 threads x 4 floats per unit
-        if (t < P * 48) {
+        if (t < np * 48) {
             const int i = t / 48, part = (t % 48) >> 4, q4 = t & 15;
             const float4 v = __ldcg(reinterpret_cast<const float4*>(a.qkv + (size_t)sm.um[i] * kQkv + part * kWidth +
                                                                     sm.uh[i] * kHeadDim) + q4);
             *reinterpret_cast<float4*>(&sm.qkvh[i][part * kHeadDim + 4 * q4]) = v;
         }
-        __syncthreads();
+        csync();
         // virtual warp `warp` of every unit: the batch-1 per-warp online softmax
 #pragma unroll 1
-        for (int i = 0; i < P; ++i) {
+        for (int i = 0; i < np; ++i) {
             const uint32_t m = sm.um[i], h = sm.uh[i], c = sm.uc[i];
             const uint32_t S = sm.units.S[m], ch = sm.units.ch[m], keys = S + 1;
             const uint32_t k0 = c * ch, k1 = min(k0 + ch, keys);
@@ -519,9 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
             sm.vo[i][warp][2 * lane] = o.x;
             sm.vo[i][warp][2 * lane + 1] = o.y;
         }
-        __syncthreads();
+        csync();
         // merge the 16 states of each unit (warp order), write its partial, append K/V
-        if (t < P * kHeadDim) {
+        if (t < np * kHeadDim) {
             const int i = t / kHeadDim, d = t % kHeadDim;
             float M = -INFINITY;
 #pragma unroll
@@ -541,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
                 pp[1] = Ls;
             }
         }
-        for (int tt = t; tt < P * 2 * kHeadDim; tt += kThreads) {
+        for (int tt = t; tt < np * 2 * kHeadDim; tt += kThreads) {
             const int i = tt / (2 * kHeadDim), r = tt % (2 * kHeadDim);
             const uint32_t m = sm.um[i];
             if (sm.uc[i] == sm.units.nch[m] - 1) {
@@ -549,18 +581,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
                 dst[r % kHeadDim] = sm.qkvh[i][kHeadDim + r];
             }
         }
-        __syncthreads();
-        if (t < P) {
+        csync();
+        if (t < np) {
             const uint32_t m = sm.um[t];
             unsigned* cnt = a.head_cnt + ((size_t)li * kMaxBatch + m) * kHeads + sm.uh[t];
             unsigned old;
             asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
             const bool last = old == sm.units.nch[m] - 1;
-            if (last) *reinterpret_cast<volatile unsigned*>(cnt) = 0;  // next use: a later launch
+            if (last) *reinterpret_cast<volatile unsigned*>(cnt) = 0;  // next use: after a grid-wide hand-off
             sm.last[t] = last;
         }
-        __syncthreads();
-        if (t < P * kHeadDim) {  // last unit of (row, head): merge its partials in chunk order
+        csync();
+        if (t < np * kHeadDim) {  // last unit of (row, head): merge its partials in chunk order
             const int i = t / kHeadDim, d = t % kHeadDim;
             if (sm.last[i]) {
                 const uint32_t m = sm.um[i], h = sm.uh[i], nch = sm.units.nch[m];
@@ -588,18 +620,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
                 a.attn[(size_t)m * kWidth + h * kHeadDim + d] = O / Ls;
             }
         }
-        __syncthreads();
+        csync();
     }
 }
 
-// ------------------------------------------------------------ GEMV phases
-enum BatchPhase : int { kBQkv = 0, kBOproj, kBFc, kBMp, kBHead };
-
-// Thread 0: L2 prefetch of the cached K/V of the attention units this CTA
-// will run for layer li (the batched form of prefetch_attn_kv).
-__device__ void bprefetch_kv(const BatchArgs& a, int cta, int ncta, int li, uint32_t fwd) {
-    BUnits u;
-    batch_units(a, ncta, fwd, u);
+// L2 prefetch of the cached K/V rows of the attention units this CTA will run
+// for layer li, issued by all consumer threads (one 128-byte line each, no
+// bulk-copy queue involved) at the start of the c_attn phase, so the
+// attention phase reads them from L2.
+__device__ void bprefetch_kv(const BatchArgs& a, int cta, int ncta, int li, uint32_t act, uint32_t gstep,
+                             BUnits& u) {
+    if (threadIdx.x == 0) batch_units(a, ncta, act, gstep, u);
+    csync();
     const uint32_t total = u.start[a.M];
     for (uint32_t x = cta; x < total; x += ncta) {
         uint32_t m = 0;
@@ -607,20 +639,108 @@ __device__ void bprefetch_kv(const BatchArgs& a, int cta, int ncta, int li, uint
         const uint32_t r = x - u.start[m], h = r / u.nch[m], c = r % u.nch[m];
         const uint32_t k0 = c * u.ch[m], k1 = min(k0 + u.ch[m], u.S[m]);
         if (k1 <= k0) continue;
-        const uint32_t bytes = (k1 - k0) * kHeadDim * 4;
-        for (int kv = 0; kv < 2; ++kv)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(arena_kv(a, m, li, kv, h) +
-                                                                              (size_t)k0 * kHeadDim),
-                         "r"(bytes)
-                         : "memory");
+        const uint32_t lines = 4 * (k1 - k0);  // K and V, two lines per 64-float row
+        for (uint32_t l = threadIdx.x; l < lines; l += kThreads) {
+            const uint32_t kv = l / (2 * (k1 - k0)), rem = l % (2 * (k1 - k0));
+            const float* p = arena_kv(a, m, li, (int)kv, h) + (size_t)(k0 + (rem >> 1)) * kHeadDim + (rem & 1) * 32;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+        }
     }
+}
+
+// ------------------------------------------------------------ GEMV phases
+enum BatchPhase : int { kBQkv = 0, kBOproj, kBFc, kBMp, kBHead };
+
+// The repetition penalty and temperature of one logit (score_scale) with the
+// row's history set read from global memory.
+__device__ __forceinline__ float score_scale_global(float s, uint32_t i, const uint32_t* seen, const SampleOpts& o) {
+    if (o.rp != 1.0f && ((__ldcg(seen + (i >> 5)) >> (i & 31)) & 1u)) s = s < 0.0f ? s * o.rp : s / o.rp;
+    if (o.temperature != 1.0f) s = s / o.temperature;
+    return s;
+}
+
+// One GEMV phase of layer li (li = layers: the head) for the active rows whose
+// fed codes were drawn at global step gstep.  Consumer threads only.
+template <int PH, int G>
+__device__ bool bgemv_phase(BCtx& cx, int li, uint32_t act, uint32_t gstep) {
+    const BatchArgs& a = cx.a;
+    const Rows& rows = cx.rows;
+    if (PH == kBQkv) {
+        bprefetch_kv(a, cx.cta, cx.ncta, li, act, gstep, cx.sm.at.units);
+        const LayerW& lw = cx.w.layer[li];
+        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
+        ln_load(lw.ln1_g, lw.ln1_b, gv, bv);
+        load_rows<G>(cx, a.x, kWidth, li == 0, act, gstep, x);
+        layernorm_rows(x, gv, bv, cx.sm.wstat);
+        const int r0 = rows.q0;
+        return bgemv_1280<G>(cx, rows.q1 - r0, x, act, 40 + li, [&](int row, int m, float v) {
+            a.qkv[(size_t)m * kQkv + r0 + row] = v + __ldg(lw.b_qkv + r0 + row);
+        });
+    } else if (PH == kBOproj) {
+        const LayerW& lw = cx.w.layer[li];
+        float2 x[kMPG][kVec];
+        load_rows<G>(cx, a.attn, kWidth, false, act, gstep, x);
+        const int r0 = rows.o0;
+        return bgemv_1280<G>(cx, rows.o1 - r0, x, act, 70 + li, [&](int row, int m, float v) {
+            const int r = r0 + row;
+            float res;
+            if (li == 0) {
+                const uint32_t tok = __ldcg(&a.st->token[m]), pos = 2 + row_fwd(a, m, gstep);
+                res = __ldg(cx.w.mel_emb + (size_t)tok * kWidth + r) + __ldg(cx.w.mel_pos + (size_t)pos * kWidth + r);
+            } else {
+                res = __ldcg(a.x + (size_t)m * kWidth + r);
+            }
+            a.hm[(size_t)m * kWidth + r] = res + (v + __ldg(lw.b_o + r));
+        });
+    } else if (PH == kBFc) {
+        const LayerW& lw = cx.w.layer[li];
+        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
+        ln_load(lw.ln2_g, lw.ln2_b, gv, bv);
+        load_rows<G>(cx, a.hm, kWidth, false, act, gstep, x);
+        layernorm_rows(x, gv, bv, cx.sm.wstat);
+        const int f0 = rows.f0;
+        return bgemv_1280<G>(cx, rows.f1 - f0, x, act, 130 + li, [&](int row, int m, float v) {
+            a.f[(size_t)m * kFfn + f0 + row] = gelu_ref(v + __ldg(lw.b_fc + f0 + row));
+        });
+    } else if (PH == kBMp) {
+        const LayerW& lw = cx.w.layer[li];
+        const int r0 = rows.o0;
+        return bgemv_long<G>(cx, rows.o1 - r0, act, 160 + li, [&](int row, int m, float v) {
+            const int r = r0 + row;
+            const float res = __ldcg(a.hm + (size_t)m * kWidth + r);
+            a.x[(size_t)m * kWidth + r] = res + (v + __ldg(lw.b_mp + r));
+        });
+    } else {  // head: ln_f -> final_norm -> mel_head (gpt.cpp:120-122)
+        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
+        ln_load(cx.w.lnf_g, cx.w.lnf_b, gv, bv);
+        load_rows<G>(cx, a.x, kWidth, false, act, gstep, x);
+        layernorm_rows(x, gv, bv, cx.sm.wstat);
+        ln_load(cx.w.fn_g, cx.w.fn_b, gv, bv);
+        csync();  // the next LayerNorm reuses wstat
+        layernorm_rows(x, gv, bv, cx.sm.wstat);
+        const int r0 = rows.h0;
+        return bgemv_1280<G>(cx, rows.h1 - r0, x, act, 201, [&](int row, int m, float v) {
+            const uint32_t r = r0 + row;
+            const float s = v + __ldg(cx.w.b_head + r);
+            a.logits[(size_t)m * kBatchLogitsStride + r] =
+                a.scaled_head ? score_scale_global(s, r, a.seen + (size_t)m * kSeenWords, a.opts[m]) : s;
+        });
+    }
+}
+
+// ------------------------------------------------------------ layered path
+// Codes fed by a layered forward step: drawn at global step st->step - 1 (the
+// sampler kernel advanced st->step after its draw).
+__device__ __forceinline__ uint32_t layered_gstep(const BatchArgs& a) {
+    return (uint32_t)ld_volatile((const int*)&a.st->step) - 1u;
 }
 
 template <int PH, int G>
 __global__ void __launch_bounds__(kCtaThreads, 1) k_bgemv(BatchArgs a, int li) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     BatchSmem& sm = *reinterpret_cast<BatchSmem*>(smem_raw);
-    if (ld_volatile((const int*)&a.st->active) == 0) return;
+    const uint32_t act = rows_active(a);
+    if (act == 0) return;
     const int cta = blockIdx.x, ncta = gridDim.x;
     const Rows rows = cta_rows(cta, ncta);
     load_table(sm.w, a.d.w);
@@ -634,70 +754,138 @@ __global__ void __launch_bounds__(kCtaThreads, 1) k_bgemv(BatchArgs a, int li) {
         return;
     }
     BCtx cx{a, sm.w, sm.ring, sm, rows, cta, ncta, 0};
-    const uint32_t fwd = fwd_index(a.st), pos = 2 + fwd;
-    const int t = threadIdx.x;
-    if (PH == kBQkv) {
-        if (t == 0) bprefetch_kv(a, cta, ncta, li, fwd);
-        const LayerW& lw = sm.w.layer[li];
-        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
-        ln_load(lw.ln1_g, lw.ln1_b, gv, bv);
-        load_rows<G>(cx, a.x, kWidth, li == 0, pos, x);
-        layernorm_rows(x, gv, bv, sm.wstat);
-        const int r0 = rows.q0;
-        bgemv_1280<G>(cx, rows.q1 - r0, x, 40 + li, [&](int row, int m, float v) {
-            a.qkv[(size_t)m * kQkv + r0 + row] = v + __ldg(lw.b_qkv + r0 + row);
-        });
-    } else if (PH == kBOproj) {
-        const LayerW& lw = sm.w.layer[li];
-        float2 x[kMPG][kVec];
-        load_rows<G>(cx, a.attn, kWidth, false, pos, x);
-        const int r0 = rows.o0;
-        bgemv_1280<G>(cx, rows.o1 - r0, x, 70 + li, [&](int row, int m, float v) {
-            const int r = r0 + row;
-            float res;
-            if (li == 0) {
-                const uint32_t tok = a.st->token[m];
-                res = __ldg(sm.w.mel_emb + (size_t)tok * kWidth + r) + __ldg(sm.w.mel_pos + (size_t)pos * kWidth + r);
-            } else {
-                res = __ldcg(a.x + (size_t)m * kWidth + r);
+    bgemv_phase<PH, G>(cx, li, act, layered_gstep(a));
+    if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_battn(BatchArgs a, int li) {
+    __shared__ BAttnSmem<kUnitsLayered> sm;
+    const uint32_t act = rows_active(a);
+    if (act == 0) return;
+    battn_phase<kUnitsLayered>(a, li, act, layered_gstep(a), blockIdx.x, gridDim.x, sm);
+}
+
+// --------------------------------------------------------- persistent path
+// Grid barrier of k_bdecode (all CTAs co-resident by the cooperative launch),
+// as grid_barrier: release add, acquire poll by thread 0, bounded; true when
+// the kernel must abort.
+__device__ bool bgrid_barrier(BCtx& cx, unsigned& target, int where) {
+    target += gridDim.x;
+    csync();
+    if (threadIdx.x == 0) {
+        unsigned* bar = &cx.a.d.b.ctl->bar;
+        int* status = cx.a.d.b.ctl->status;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        int abort = 0;
+        if (ld_acquire_gpu(bar) < target) {
+            const unsigned long long t0 = globaltimer_ns();
+            for (unsigned spins = 1; ld_acquire_gpu(bar) < target; ++spins) {
+                if ((spins & 31u) == 0) {
+                    const unsigned long long dt = globaltimer_ns() - t0;
+                    if (dt > kStatusPollNs && ld_volatile(status) != 0) {
+                        abort = 1;
+                        break;
+                    }
+                    if (dt > wait_limit(cx.a.d)) {
+                        set_status(status, kStatusBarrierTimeout, where, (int)target);
+                        abort = 1;
+                        break;
+                    }
+                }
             }
-            a.hm[(size_t)m * kWidth + r] = res + (v + __ldg(lw.b_o + r));
-        });
-    } else if (PH == kBFc) {
-        const LayerW& lw = sm.w.layer[li];
-        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
-        ln_load(lw.ln2_g, lw.ln2_b, gv, bv);
-        load_rows<G>(cx, a.hm, kWidth, false, pos, x);
-        layernorm_rows(x, gv, bv, sm.wstat);
-        const int f0 = rows.f0;
-        bgemv_1280<G>(cx, rows.f1 - f0, x, 130 + li, [&](int row, int m, float v) {
-            a.f[(size_t)m * kFfn + f0 + row] = gelu_ref(v + __ldg(lw.b_fc + f0 + row));
-        });
-    } else if (PH == kBMp) {
-        const LayerW& lw = sm.w.layer[li];
-        const int r0 = rows.o0;
-        bgemv_long<G>(cx, rows.o1 - r0, 160 + li, [&](int row, int m, float v) {
-            const int r = r0 + row;
-            const float res = __ldcg(a.hm + (size_t)m * kWidth + r);
-            a.x[(size_t)m * kWidth + r] = res + (v + __ldg(lw.b_mp + r));
-        });
-    } else {  // head: ln_f -> final_norm -> mel_head (gpt.cpp:120-122)
-        float2 gv[kVec], bv[kVec], x[kMPG][kVec];
-        ln_load(sm.w.lnf_g, sm.w.lnf_b, gv, bv);
-        load_rows<G>(cx, a.x, kWidth, false, pos, x);
-        layernorm_rows(x, gv, bv, sm.wstat);
-        ln_load(sm.w.fn_g, sm.w.fn_b, gv, bv);
-        csync();  // the next LayerNorm reuses wstat
-        layernorm_rows(x, gv, bv, sm.wstat);
-        const int r0 = rows.h0;
-        bgemv_1280<G>(cx, rows.h1 - r0, x, 201, [&](int row, int m, float v) {
-            const uint32_t r = r0 + row;
-            const float s = v + __ldg(sm.w.b_head + r);
-            a.logits[(size_t)m * kBatchLogitsStride + r] =
-                a.scaled_head ? score_scale(s, r, a.seen + (size_t)m * kSeenWords, a.opts[m]) : s;
-        });
+        }
+        cx.sm.abort = abort;
+    }
+    csync();
+    return cx.sm.abort != 0;
+}
+
+// Draw `gstep` of row m (one CTA): the processors and the token choice of the
+// batch-1 loop (sample_next) on the row's logits, then the row's bookkeeping:
+// code, count, stop (gpt_sampling.cpp:178-187), repetition-penalty set.  In
+// its own frame so its registers do not constrain the phases.
+__device__ __noinline__ void bsample_row(const BatchArgs& a, uint32_t m, uint32_t gstep, SamplerSmem& sa) {
+    int* status = a.d.b.ctl->status;
+    uint32_t* seen = a.seen + (size_t)m * kSeenWords;
+    for (int k = threadIdx.x; k < kBits; k += kThreads) sa.seen[k] = __ldcg(seen + k);
+    csync();
+    const uint32_t i = gstep - a.st->base[m];
+    const SampleOpts& o = a.opts[m];
+    // draw 0 reads the prefill's raw logits; later draws read the head's scaled scores
+    const uint32_t token = run_sampler(a.logits + (size_t)m * kBatchLogitsStride, o, i, o.do_sample == 0, sa,
+                                       a.big + m, nullptr, status, a.scaled_head && i > 0);
+    if (threadIdx.x == 0) {
+        BatchState* st = a.st;
+        const uint32_t bit = 1u << m;
+        if (token == (uint32_t)kStopCode) {
+            st->stopped[m] = 1;
+            atomicAnd(&st->active, ~bit);
+        } else if (token >= (uint32_t)kStartCode) {
+            if (token != 0xffffffffu) set_status(status, kStatusInvalidCode, 300, (int)token);
+            atomicAnd(&st->active, ~bit);
+        } else {
+            a.codes[(size_t)m * a.codes_stride + i] = token;
+            st->n_codes[m] = i + 1;
+            st->token[m] = token;
+            atomicOr(&seen[token >> 5], 1u << (token & 31));
+            if (i + 1 >= st->maxc[m]) atomicAnd(&st->active, ~bit);
+        }
+    }
+    csync();
+}
+
+// `iters` batched steps in one cooperative launch.  With `sample`, step it
+// draws the next code of every active row (CTA m samples row m) and feeds the
+// codes to one forward step; it ends early once no row is active.  Without,
+// one forward step feeds the codes already in the state (drawn at global step
+// st->step - 1: beam search).  The producer warp streams the weights of the
+// forward steps one after another through the ring.
+template <int G>
+__global__ void __launch_bounds__(kCtaThreads, 1) k_bdecode(BatchArgs a, uint32_t iters, int sample) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    BatchSmem& sm = *reinterpret_cast<BatchSmem*>(smem_raw);
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    const Rows rows = cta_rows(cta, ncta);
+    load_table(sm.w, a.d.w);
+    if (threadIdx.x == 0) {
+        sm.abort = 0;
+        ring_init(sm.ring);
+    }
+    __syncthreads();
+    if (threadIdx.x >= kThreads) {  // producer warp
+        if (threadIdx.x == kThreads) producer(a.d, sm.w, sm.ring, rows, 0, segs_per_step(sm.w), (int)iters);
+        return;
+    }
+    BCtx cx{a, sm.w, sm.ring, sm, rows, cta, ncta, 0};
+    const int L = sm.w.layers;
+    unsigned target = 0;
+    const uint32_t step0 = (uint32_t)ld_volatile((const int*)&a.st->step);
+    uint32_t draws = 0;
+    for (uint32_t it = 0; it < iters; ++it) {
+        uint32_t gstep = step0 - 1u;
+        if (sample) {
+            gstep = step0 + it;
+            const uint32_t act0 = rows_active(a);
+            if ((uint32_t)cta < a.M && ((act0 >> cta) & 1u)) bsample_row(a, cta, gstep, sm.sa);
+            ++draws;
+            if (bgrid_barrier(cx, target, 990)) break;
+        }
+        const uint32_t act = rows_active(a);
+        if (act == 0) break;
+        bool ok = true;
+        for (int li = 0; li < L && ok; ++li) {
+            ok = bgemv_phase<kBQkv, G>(cx, li, act, gstep) && !bgrid_barrier(cx, target, 1000 + li);
+            if (!ok) break;
+            battn_phase<kUnitsPersistent>(a, li, act, gstep, cta, ncta, sm.at);
+            ok = !bgrid_barrier(cx, target, 1100 + li) && bgemv_phase<kBOproj, G>(cx, li, act, gstep) &&
+                 !bgrid_barrier(cx, target, 1200 + li) && bgemv_phase<kBFc, G>(cx, li, act, gstep) &&
+                 !bgrid_barrier(cx, target, 1300 + li) && bgemv_phase<kBMp, G>(cx, li, act, gstep) &&
+                 !bgrid_barrier(cx, target, 1400 + li);
+        }
+        if (!ok || !bgemv_phase<kBHead, G>(cx, L, act, gstep) || bgrid_barrier(cx, target, 1500)) break;
     }
     if (threadIdx.x == 0) ring_finish(sm.ring, cx.k);
+    if (sample && cta == 0 && threadIdx.x == 0) a.st->step = step0 + draws;
 }
 
 // ------------------------------------------------------------ host side
@@ -715,12 +903,14 @@ cudaError_t set_bgemv_smem() {
 
 cudaError_t batch_configure() {
     cudaError_t e = cudaSuccess;
-#define ITTS_CFG(G)                                         \
-    if (e == cudaSuccess) e = set_bgemv_smem<kBQkv, G>();   \
-    if (e == cudaSuccess) e = set_bgemv_smem<kBOproj, G>(); \
-    if (e == cudaSuccess) e = set_bgemv_smem<kBFc, G>();    \
-    if (e == cudaSuccess) e = set_bgemv_smem<kBMp, G>();    \
-    if (e == cudaSuccess) e = set_bgemv_smem<kBHead, G>();
+#define ITTS_CFG(G)                                                                                             \
+    if (e == cudaSuccess) e = set_bgemv_smem<kBQkv, G>();                                                      \
+    if (e == cudaSuccess) e = set_bgemv_smem<kBOproj, G>();                                                    \
+    if (e == cudaSuccess) e = set_bgemv_smem<kBFc, G>();                                                       \
+    if (e == cudaSuccess) e = set_bgemv_smem<kBMp, G>();                                                       \
+    if (e == cudaSuccess) e = set_bgemv_smem<kBHead, G>();                                                     \
+    if (e == cudaSuccess)                                                                                      \
+        e = cudaFuncSetAttribute(k_bdecode<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(BatchSmem));
     ITTS_BATCH_GROUPS(ITTS_CFG)
 #undef ITTS_CFG
     return e;
@@ -741,11 +931,13 @@ void launch_batch_layers(const BatchArgs& a, int layers, int ncta, cudaStream_t 
     *launches += 1;
 }
 
-// One forward step of the M rows (the codes in a.st->token) through every
-// layer and the head: 5 launches per layer + 1.
+__host__ __forceinline__ int batch_groups(uint32_t M) { return (int(M) + kMPG - 1) / kMPG; }
+
+// Layered path: one forward step of the active rows (codes drawn at global
+// step st->step - 1) through every layer and the head: 5 launches per layer + 1.
 cudaError_t launch_batch_forward(const BatchArgs& a, int layers, int ncta, cudaStream_t s, uint64_t* launches) {
-    const int G = (int(a.M) + kMPG - 1) / kMPG;
     if (a.M < 1 || a.M > (uint32_t)kMaxBatch) return cudaErrorInvalidValue;
+    const int G = batch_groups(a.M);
     if (G <= 1) launch_batch_layers<1>(a, layers, ncta, s, launches);
     else if (G <= 2) launch_batch_layers<2>(a, layers, ncta, s, launches);
     else if (G <= 4) launch_batch_layers<4>(a, layers, ncta, s, launches);
@@ -753,6 +945,29 @@ cudaError_t launch_batch_forward(const BatchArgs& a, int layers, int ncta, cudaS
     else launch_batch_layers<8>(a, layers, ncta, s, launches);
 #endif
     return cudaGetLastError();
+}
+
+template <int G>
+cudaError_t launch_bdecode(const BatchArgs& a, uint32_t iters, int sample, int ncta, cudaStream_t s) {
+    BatchArgs copy = a;
+    void* args[] = {&copy, &iters, &sample};
+    return cudaLaunchCooperativeKernel((const void*)k_bdecode<G>, dim3(ncta), dim3(kCtaThreads), args,
+                                       sizeof(BatchSmem), s);
+}
+
+// Persistent path: `iters` steps (sample = 1: draw + forward; sample = 0: one
+// forward of the codes in the state) in one cooperative launch.
+cudaError_t launch_batch_persistent(const BatchArgs& a, uint32_t iters, int sample, int ncta, cudaStream_t s) {
+    if (a.M < 1 || a.M > (uint32_t)kMaxBatch) return cudaErrorInvalidValue;
+    const int G = batch_groups(a.M);
+    if (G <= 1) return launch_bdecode<1>(a, iters, sample, ncta, s);
+    if (G <= 2) return launch_bdecode<2>(a, iters, sample, ncta, s);
+    if (G <= 4) return launch_bdecode<4>(a, iters, sample, ncta, s);
+#if ITTS_WBF16
+    return launch_bdecode<8>(a, iters, sample, ncta, s);
+#else
+    return cudaErrorInvalidValue;
+#endif
 }
 
 }  // namespace ITTS_WNS

@@ -165,6 +165,19 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
         : "memory");
     return done != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase does not complete
+// is woken after about `ns` nanoseconds instead of the hardware's default
+// suspend limit (about a millisecond), so a loop around it notices a stop
+// request promptly.
+__device__ __forceinline__ bool mbar_try_wait_hint(unsigned long long* bar, uint32_t parity, uint32_t ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return done != 0;
+}
 // L2 policy of the streamed weights: evicted first, so that one step's 1.9 GB
 // sweep does not push the KV cache, the activations and the kernel's own
 // instructions out of L2.
@@ -276,20 +289,22 @@ __device__ __forceinline__ bool pf_advance(const ModelW& w, const Rows& rows, in
 // Bounded wait of the producer for a slot's previous use to be handed back;
 // while it waits it keeps the L2 prefetch kPfAhead bytes ahead of the ring.
 // False when the consumers raised `stop`, on an error status or on timeout.
+// The schedule can outlast the consumers (a loop that ends on the stop code),
+// so `stop` is checked after every try, and each try sleeps at most ~1 us.
 __device__ bool wait_empty(Ring& R, int s, uint32_t parity, const DecodeArgs& a, uint32_t j, const ModelW& w,
                            const Rows& rows, int k0, int k1, int n_steps, PfCursor& pf, unsigned long long issued) {
-    if (mbar_try_wait(&R.empty[s], parity)) return true;
+    if (mbar_try_wait_hint(&R.empty[s], parity, 1000)) return true;
     int* status = a.b.ctl->status;
     const unsigned long long t0 = globaltimer_ns();
     bool more = true;
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(&R.empty[s], parity)) return true;
+        if (mbar_try_wait_hint(&R.empty[s], parity, 1000)) return true;
+        if (R.stop) return false;
         if (more && pf.pos < issued + kPfAhead) {
             more = pf_advance(w, rows, k0, k1, n_steps, pf, pf.pos >= issued);
             continue;
         }
         if ((i & 63u) == 0) {
-            if (R.stop) return false;
             const unsigned long long dt = globaltimer_ns() - t0;
             if (dt > kStatusPollNs && ld_volatile(status) != 0) return false;
             if (dt > wait_limit(a)) {

@@ -600,11 +600,41 @@ void batch_prefill(itts_gpt_ctx* c, const float* prefix, size_t n_floats, uint32
     ++c->launches;
 }
 
+// One forward step of the rows in the state (codes drawn at global step
+// st.step - 1): the persistent kernel, or in layered mode one launch per phase.
 void batch_forward(itts_gpt_ctx* c, const itts::BatchArgs& a) {
+    if (c->mode == 0) {
+        reset_ctl(c);  // grid-barrier counter
+        ck(c->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_batch_persistent(a, 1, 0, c->sm_count, c->stream)
+                                         : itts::wf32::launch_batch_persistent(a, 1, 0, c->sm_count, c->stream),
+           "batched decode launch");
+        ++c->launches;
+        return;
+    }
     ck(c->dtype == ITTS_WEIGHTS_BF16
            ? itts::wbf16::launch_batch_forward(a, int(c->layers), c->sm_count, c->stream, &c->launches)
            : itts::wf32::launch_batch_forward(a, int(c->layers), c->sm_count, c->stream, &c->launches),
        "batched forward launch");
+}
+
+// `iters` draws of every active row, each followed by a forward step while a
+// row is active (persistent kernel; layered mode: one sampler launch and one
+// forward per iteration).
+void batch_generate(itts_gpt_ctx* c, const itts::BatchArgs& a, uint32_t iters) {
+    if (c->mode == 0) {
+        reset_ctl(c);
+        ck(c->dtype == ITTS_WEIGHTS_BF16 ? itts::wbf16::launch_batch_persistent(a, iters, 1, c->sm_count, c->stream)
+                                         : itts::wf32::launch_batch_persistent(a, iters, 1, c->sm_count, c->stream),
+           "batched decode launch");
+        ++c->launches;
+        return;
+    }
+    for (uint32_t i = 0; i < iters; ++i) {
+        ck(itts::launch_batch_sample(a, c->stream), "batched sampler launch");
+        ++c->launches;
+        if (i + 1 == iters) break;
+        batch_forward(c, a);
+    }
 }
 
 // Device-time marks of a generate call (events on the context's stream):
@@ -645,20 +675,16 @@ void generate_rows(itts_gpt_ctx* c, size_t M, const float* const* prefixes, cons
     for (size_t m = 0; m < M; ++m) {
         st.s0[m] = uint32_t(n_floats[m] / kW);
         st.arena[m] = uint32_t(m);
+        st.maxc[m] = max_tokens;
         for (uint32_t t : {1u, 8192u}) seen[m * kSeenWords + (t >> 5)] |= 1u << (t & 31);
     }
     st.active = (1u << M) - 1;
     put_state(c);
     ck(cudaMemcpyAsync(c->bargs.seen, seen.data(), seen.size() * 4, cudaMemcpyHostToDevice, c->stream), "seen upload");
     BatchArgs a = batch_args(c, uint32_t(M), o, true);
-    a.max_codes = max_tokens;
+    a.codes_stride = max_tokens;
     mark(c, 1);
-    for (uint32_t i = 0; i < max_tokens; ++i) {
-        ck(launch_batch_sample(a, c->stream), "batched sampler launch");
-        ++c->launches;
-        if (i + 1 == max_tokens) break;
-        batch_forward(c, a);
-    }
+    batch_generate(c, a, max_tokens);
     mark(c, 2);
     std::vector<uint32_t> out(size_t(M) * max_tokens);
     ck(cudaMemcpyAsync(out.data(), c->bargs.codes, out.size() * 4, cudaMemcpyDeviceToHost, c->stream), "codes read");

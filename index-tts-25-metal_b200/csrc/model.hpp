@@ -115,15 +115,19 @@ constexpr int kMaxBatch = 16;
 // step.
 struct BatchState {
     uint32_t token[kMaxBatch];    // code each row feeds to the next forward step
-    uint32_t s0[kMaxBatch];       // cached tokens of the row before forward step 0
+    uint32_t s0[kMaxBatch];       // cached tokens of the row before its first forward step
     uint32_t arena[kMaxBatch];    // KV arena of the row
     uint32_t n_codes[kMaxBatch];  // codes generated so far
     uint32_t stopped[kMaxBatch];  // 1 when the stop code ended the row
+    uint32_t base[kMaxBatch];     // global step of the row's draw 0 (rows join at different steps)
+    uint32_t maxc[kMaxBatch];     // codes the row may generate
     uint32_t active;              // bit m: row m still decodes
-    uint32_t step;                // index of the next draw; forward step step-1 feeds token[]
-    uint32_t sample_arrivals;     // sampler CTAs that finished the current draw
+    uint32_t step;                // global index of the next draw; a row's draw i is step base + i
+    uint32_t sample_arrivals;     // sampler CTAs that finished the current draw (layered mode)
     uint32_t pad[5];
 };
+// A row's draw i feeds its code to forward step i: mel position 2 + i over
+// s0 + i cached tokens (gpt_sampling.cpp:184-186).
 
 struct BatchArgs {
     DecodeArgs d;      // weight table, status word, wait limit (ring and waits of the shared code)
@@ -139,8 +143,8 @@ struct BatchArgs {
     float* kv;         // arena 0; arena a starts at kv + a * arena_floats
     size_t arena_floats;
     BatchState* st;
-    uint32_t* codes;   // generate: [kMaxBatch][max_codes]
-    uint32_t max_codes;
+    uint32_t* codes;   // generate: code i of row m at codes[m * codes_stride + i]
+    uint32_t codes_stride;
     uint32_t* seen;    // [kMaxBatch][257] repetition-penalty sets
     SamplerBig* big;   // [kMaxBatch] sampler workspaces
     SampleOpts opts[kMaxBatch];
@@ -163,6 +167,8 @@ constexpr int kSeenWords = 257;  // ceil(8194 / 32)
     cudaError_t batch_configure();                                                                             \
     cudaError_t launch_batch_forward(const BatchArgs& a, int layers, int ncta, cudaStream_t s,                 \
                                      uint64_t* launches);                                                      \
+    cudaError_t launch_batch_persistent(const BatchArgs& a, uint32_t iters, int sample, int ncta,              \
+                                        cudaStream_t s);                                                       \
     }
 ITTS_DECLARE_DECODE_LAUNCHERS(wf32)
 ITTS_DECLARE_DECODE_LAUNCHERS(wbf16)

@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_beam_scores(const float* logits
         if (k < cnt) out[base + k] = out[base + k] + beam_score;
 }
 
-// Batched generate loop, draw st->step of every active row (one CTA per row):
+// Layered batched generate loop, global draw st->step of every active row (one
+// CTA per row; row m's draw index is st->step - base[m]):
 // the processors and the token choice of the batch-1 loop (k_decode's
 // sample_next) on the row's logits, then the row's bookkeeping -- code,
 // count, stop (gpt_sampling.cpp:178-187) and repetition-penalty set.  The last
@@ -133,7 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_batch_sample(BatchArgs a) {
     SamplerBig* big = reinterpret_cast<SamplerBig*>(smem_raw + kSamplerSmallBytes);
     BatchState* st = a.st;
     const uint32_t m = blockIdx.x;
-    const uint32_t i = (uint32_t)ld_volatile((const int*)&st->step);
+    const uint32_t gstep = (uint32_t)ld_volatile((const int*)&st->step);
+    const uint32_t i = gstep - st->base[m];
     const bool active = (ld_volatile((const int*)&st->active) >> m) & 1;
     int* status = a.d.b.ctl->status;
     if (active) {
@@ -153,11 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_batch_sample(BatchArgs a) {
                 if (token != 0xffffffffu) set_status(status, kStatusInvalidCode, 300, (int)token);
                 atomicAnd(&st->active, ~bit);
             } else {
-                a.codes[(size_t)m * a.max_codes + i] = token;
+                a.codes[(size_t)m * a.codes_stride + i] = token;
                 st->n_codes[m] = i + 1;
                 st->token[m] = token;
                 atomicOr(&seen[token >> 5], 1u << (token & 31));
-                if (i + 1 == a.max_codes) atomicAnd(&st->active, ~bit);
+                if (i + 1 >= st->maxc[m]) atomicAnd(&st->active, ~bit);
             }
         }
     }
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_batch_sample(BatchArgs a) {
         const uint32_t old = atomicAdd(&st->sample_arrivals, 1u);
         if (old == a.M - 1) {
             st->sample_arrivals = 0;
-            st->step = i + 1;
+            st->step = gstep + 1;
         }
     }
 }
