@@ -1,17 +1,29 @@
 """Benchmark of the IndexTTS 2.5 GPT decode loop on B200.
 
-Workload: 24-layer UnifiedVoice GPT, fp32,
-random-init weights (seed 42, stop code masked), prefix of 32 N(0,1)
-conditioning latents + 200 text tokens (235 rows), sampled decode T 0.8,
-top-k 30, top-p 0.8, repetition penalty 10, Philox stream seed 1234, 1024
-generated codes at batch 1.  One step = one request: prefill + the 1024-code
-token loop.  Multi-GPU: one replica per GPU (weak scaling, no collective on
-the data path); each rank serves its own request.
+Workloads (24-layer UnifiedVoice GPT, fp32, random-init
+weights seed 42, stop code masked so every request runs to its length):
+  --config 1 (default, the headline)  sampled decode T 0.8, top-k 30, top-p
+      0.8, rp 10, Philox seed 1234; prefix 32 N(0,1) latents + 200 text tokens
+      (235 rows); 1024 codes at batch 1.  One step = one request.
+  --config 0        greedy (rp 10), prefix 32 latents + 64 text tokens, 256 codes.
+  --config 2        8 independent sampled requests (text lengths U[40,300],
+                    600 codes each) decoded together by generate_batch.
+  --config 2beam    3-beam greedy search, text length from U[40,300], 600 codes.
+  --config 3        prefill-heavy: 32 latents + 16 emotion rows + 400 text
+                    tokens (451 rows), prefill then 128 sampled codes.
+  --config serving  64 requests (text U[20,400], codes U[100,1500], sampled
+                    as config 1), longest-first over the ranks, each rank
+                    serving its share with continuous batching (itts_gpt_serve,
+                    16 rows in flight).
+Multi-GPU: one replica per GPU (weights replicated, no collective on the data
+path; NCCL only for the start/stop barriers and the max-over-ranks time).
 
 Arms:
-  default            our library; `value` is device-timed with the prefix
-                     resident in HBM (prefill_async + decode_async), `e2e` is
-                     the public generate() call with host buffers.
+  default            our library.  `value`: device time (CUDA events) with the
+                     prefix resident in HBM for batch-1 configs; for the
+                     batched configs the library's own CUDA-event time of the
+                     call (itts_gpt_last_timing).  `e2e`: the public call with
+                     host buffers, wall clock around it.
   --impl reference   the reference's own CPU implementation of the path
                      (oracle/_ref: src/gpt.cpp + src/gpt_sampling.cpp on the
                      CPU MetalContext; the oracle port when _ref is absent),
@@ -23,6 +35,7 @@ import argparse
 import importlib
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -35,8 +48,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GPT decode tokens/s/GPU @B=1 and 8-GPU aggregate; % of HBM roofline"
-N_LATENTS, N_TEXT, N_CODES = 32, 200, 1024
+N_LATENTS = 32
 L2_BYTES = 126 * 2 ** 20
+KV_ROW_BYTES = 2 * 1280 * 4  # K and V of one token in one layer, fp32
 
 
 def env_int(k, d):
@@ -54,33 +68,97 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+# ------------------------------------------------------------ workloads
 def conditioning(seed, n_text, text_hi=12000):
     r = np.random.default_rng(seed)
     return (r.standard_normal(192).astype(np.float32), r.standard_normal(1280).astype(np.float32),
             r.integers(2, text_hi, n_text).astype(np.uint32))
 
 
-def make_prefix(prepare, seed):
-    spk, emo, ids = conditioning(seed, N_TEXT)
+def latent_prefix(prepare, seed, n_text, n_latents=N_LATENTS):
+    """n_latents N(0,1) conditioning rows, then prepare()'s text and start rows."""
+    spk, emo, ids = conditioning(seed, n_text)
     p = prepare(spk, emo, ids, 3)
-    lat = np.random.default_rng(seed + 1).standard_normal((N_LATENTS, 1280)).astype(np.float32)
+    lat = np.random.default_rng(seed + 1).standard_normal((n_latents, 1280)).astype(np.float32)
     return np.ascontiguousarray(np.concatenate([lat, p[3:]], 0))
 
 
-def bundle_path():
-    mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
-    cache = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
-    path = os.path.join(cache, "gpt_s42_l24_m1")
-    mit2.write_synthetic_gpt_bundle(path, seed=42, layers=24, mask_stop=True)
-    return path
+def config3_prefix(prepare, seed=3003):
+    """32 latents + 16 N(0,1) emotion-conditioning rows + 400 text rows + start row."""
+    spk, emo, ids = conditioning(seed, 400)
+    p = prepare(spk, emo, ids, 3)
+    r = np.random.default_rng(seed + 1)
+    lat = r.standard_normal((32, 1280)).astype(np.float32)
+    emov = r.standard_normal((16, 1280)).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([lat, emov, p[3:]], 0))
 
 
-def decode_bytes(stream_bytes, layers, rows, forward_steps):
-    """Algorithmic HBM bytes of one decode launch: per forward step the weight
-    stream plus the KV read (S cached keys) and the K/V append, fp32."""
-    kv_row = 2 * 1280 * 4 * layers
-    s0, n = rows, forward_steps
-    return n * (stream_bytes + kv_row) + kv_row * (n * s0 + n * (n - 1) // 2)
+def text_lengths(seed, n, lo=40, hi=300):
+    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+
+
+def sampled(gpt, seed):
+    return gpt.gen_opts(seed=seed, temperature=0.8, top_k=30, top_p=0.8, repetition_penalty=10.0,
+                        rng=gpt.RNG_PHILOX)
+
+
+def build_workload(name, gpt, dec, rank, world):
+    """The requests of one bench step on this rank: a dict with kind
+    ('single' | 'batch' | 'beam' | 'serve'), prefixes, options, code counts
+    and a description."""
+    if name == "0":
+        p = latent_prefix(dec.prepare, 1001 + rank, 64)
+        return {"kind": "single", "prefixes": [p], "opts": [gpt.gen_opts(do_sample=False)], "codes": [256],
+                "desc": "configs[0]: greedy decode (rp 10), prefix 32 latents + 64 text tokens, 256 codes, batch 1"}
+    if name == "1":
+        p = latent_prefix(dec.prepare, 1002 + rank, 200)
+        return {"kind": "single", "prefixes": [p], "opts": [sampled(gpt, 1234 + rank)], "codes": [1024],
+                "desc": "configs[1]: sampled decode (T 0.8, top-k 30, top-p 0.8, rp 10, Philox seed 1234), "
+                        "prefix 32 latents + 200 text tokens, 1024 codes, batch 1"}
+    if name == "3":
+        p = config3_prefix(dec.prepare, 3003 + rank)
+        return {"kind": "single", "prefixes": [p], "opts": [sampled(gpt, 1234 + rank)], "codes": [128],
+                "desc": "configs[3]: prefill-heavy, 32 latents + 16 emotion rows + 400 text tokens (451 rows), "
+                        "prefill then 128 sampled codes, batch 1"}
+    if name == "2":
+        lens = text_lengths(2100 + rank, 8)
+        ps = [latent_prefix(dec.prepare, 2200 + 8 * rank + i, int(lens[i])) for i in range(8)]
+        return {"kind": "batch", "prefixes": ps, "opts": [sampled(gpt, 1234 + 8 * rank + i) for i in range(8)],
+                "codes": [600] * 8,
+                "desc": "configs[2]: batch of 8 independent sampled requests (text U[40,300]), 600 codes each, "
+                        "decoded together (generate_batch)"}
+    if name == "2beam":
+        n_text = int(text_lengths(2002 + rank, 1)[0])
+        p = latent_prefix(dec.prepare, 2002 + rank, n_text)
+        return {"kind": "beam", "prefixes": [p], "opts": [gpt.gen_opts(do_sample=False, num_beams=3)],
+                "codes": [600], "desc": "configs[2]: greedy 3-beam search (rp 10), text U[40,300], 600 codes"}
+    if name == "serving":
+        replicas = importlib.import_module("index-tts-25-metal_b200.replicas")
+        reqs = replicas.partition(replicas.serving_requests(64), world, rank, "longest_first")
+        ps = [latent_prefix(dec.prepare, 4000 + q.index, q.text_len) for q in reqs]
+        return {"kind": "serve", "prefixes": ps, "opts": [sampled(gpt, 5000 + q.index) for q in reqs],
+                "codes": [q.codes for q in reqs], "requests": [q.index for q in reqs],
+                "desc": "configs[4]: 64 requests (text U[20,400], codes U[100,1500], sampled as configs[1]), "
+                        "longest-first over the ranks, continuous batching with 16 rows in flight per GPU"}
+    raise ValueError(name)
+
+
+def kv_read_bytes(layers, rows, forward_steps):
+    """K/V bytes the forward steps of one request read and append: step i
+    attends over rows + i cached keys and writes one more."""
+    n = forward_steps
+    return KV_ROW_BYTES * layers * (n * rows + n * (n - 1) // 2 + n)
 
 
 class ClockSampler:
@@ -143,45 +221,82 @@ def gpu_smi_id(local_rank):
         return local_rank
 
 
+def bundle_path():
+    mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+    cache = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
+    path = os.path.join(cache, "gpt_s42_l24_m1")
+    mit2.write_synthetic_gpt_bundle(path, seed=42, layers=24, mask_stop=True)
+    return path
+
+
 # --------------------------------------------------------------- CPU side
-def cpu_reference_sample(prefix, n_tokens, threads=None):
-    """Times the reference's CPU implementation (oracle/_ref, else the oracle
-    port): prefill once (untimed), then n_tokens cached decode steps through
-    GptDecoder::step.  Returns (tokens/s, kind, cores, sample description)."""
-    if threads:
-        os.environ["ORC_THREADS"] = str(threads)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    path = bundle_path()
-    cls, kind = (O.RefOracle, "reference") if O.RefOracle.available() else (O.PortOracle, "port")
-    ref = cls(path)
-    ref.prefill(prefix)
-    ref.step(5, 2)  # warm: first call transposes/caches weights in the reference
-    t0 = time.perf_counter()
-    for i in range(n_tokens):
-        ref.step(int(7 + 13 * i) % 8192, 3 + i)
-    dt = time.perf_counter() - t0
-    cores = cls.threads()
-    ref.close()
-    sample = (f"{n_tokens} cached decode steps after a {prefix.shape[0]}-row prefill "
-              f"(S {prefix.shape[0] + 1}..{prefix.shape[0] + n_tokens}), fp32, {cores} threads")
-    return n_tokens / dt, kind, cores, sample
+CPU_SAMPLE_SCRIPT = r"""
+import json, os, sys, time
+sys.path.insert(0, {oracle!r})
+import numpy as np
+import oracle as O
+cls, kind = (O.RefOracle, "reference") if O.RefOracle.available() else (O.PortOracle, "port")
+ref = cls({bundle!r})
+prefix = np.load({prefix!r})
+t0 = time.perf_counter(); ref.prefill(prefix); pre = time.perf_counter() - t0
+ref.step(5, 2)
+t0 = time.perf_counter()
+for i in range({n}):
+    ref.step(int(7 + 13 * i) % 8192, 3 + i)
+dt = time.perf_counter() - t0
+print(json.dumps({{"tokens_per_s": {n} / dt, "kind": kind, "threads": cls.threads(), "prefill_s": pre,
+                  "rows": int(prefix.shape[0])}}))
+"""
+
+
+def cpu_sample(prefix, n_tokens, threads):
+    """The reference's CPU implementation (oracle/_ref, else the oracle port)
+    in a child process with `threads` worker threads: prefill (untimed), then
+    n_tokens cached decode steps through GptDecoder::step."""
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        pf = os.path.join(d, "prefix.npy")
+        np.save(pf, prefix)
+        code = CPU_SAMPLE_SCRIPT.format(oracle=os.path.join(ROOT, "oracle"), bundle=bundle_path(), prefix=pf,
+                                        n=n_tokens)
+        env = dict(os.environ, ORC_THREADS=str(threads))
+        r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=1200)
+        if r.returncode != 0:
+            raise RuntimeError(f"CPU sample failed: {r.stderr[-2000:]}")
+        return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def cpu_baseline(prefix, args):
+    """All-core sample at the workload's own prefix, and a single-thread
+    sample after a 32-row prefix (a single-threaded prefill of hundreds of
+    rows would take minutes; decode cost per token is dominated by the 1.93 GB
+    weight sweep, the K/V share at S ~ 40 vs ~300 is about 3%)."""
+    cores = os.cpu_count() or 1
+    allc = cpu_sample(prefix, args.cpu_tokens, cores)
+    one = cpu_sample(prefix[:32], args.cpu_tokens_1t, 1)
+    rows = int(prefix.shape[0])
+    return {"value": allc["tokens_per_s"], "unit": "tokens/s", "cores": allc["threads"], "kind": allc["kind"],
+            "value_1thread": one["tokens_per_s"], "cpu_model": cpu_model(), "host_cpus": cores,
+            "sample": (f"all-core: {args.cpu_tokens} cached decode steps (GptDecoder::step) after the workload's "
+                       f"{rows}-row prefill (S {rows + 1}..{rows + args.cpu_tokens + 1}); 1 thread: "
+                       f"{args.cpu_tokens_1t} steps after a 32-row prefill (S 33..{33 + args.cpu_tokens_1t}); "
+                       "fp32, the workload's model")}
 
 
 def run_reference_arm(args):
     rank = env_int("RANK", 0)
     if rank != 0:
         return
-    cfg = {"workload": "configs[1]: sampled decode, prefix 32 latents + 200 text tokens (235 rows), "
-                       "1024 codes; reference arm = bounded decode samples", "prefix_rows": None,
-           "codes_per_request": N_CODES, "model": "UnifiedVoice GPT 24L d1280 fp32 random-init"}
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     path = bundle_path()
     cls, kind = (O.RefOracle, "reference") if O.RefOracle.available() else (O.PortOracle, "port")
     ref = cls(path)
-    prefix = make_prefix(ref.prepare, 1002)
-    cfg["prefix_rows"] = int(prefix.shape[0])
+    prefix = latent_prefix(ref.prepare, 1002, 200)
+    cfg = {"workload": "configs[1]: sampled decode, prefix 32 latents + 200 text tokens (235 rows), 1024 codes; "
+                       "reference arm = bounded decode samples", "prefix_rows": int(prefix.shape[0]),
+           "codes_per_request": 1024, "model": "UnifiedVoice GPT 24L d1280 fp32 random-init",
+           "cpu_model": cpu_model()}
     ref.prefill(prefix)
     ref.step(5, 2)
     per_step = args.ref_tokens
@@ -198,13 +313,16 @@ def run_reference_arm(args):
     total = sum(times)
     value = per_step * len(times) / total
     cores = cls.threads()
+    s_lo, s_hi = prefix.shape[0] + 2, prefix.shape[0] + 1 + pos
+    cfg["s_range"] = [int(s_lo), int(s_hi)]
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * total / len(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights)",
             "config": cfg, "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
+                             "cpu_model": cpu_model(),
                              "sample": f"each step = {per_step} cached decode steps (GptDecoder::step) of the "
-                                       f"configs[1] model after its {prefix.shape[0]}-row prefill"},
+                                       f"configs[1] model after its {prefix.shape[0]}-row prefill, S {s_lo}..{s_hi}"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -222,6 +340,7 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     gpt = importlib.import_module("index-tts-25-metal_b200.gpt")
+    replicas = importlib.import_module("index-tts-25-metal_b200.replicas")
     path = bundle_path() if rank == 0 or world == 1 else None
     if world > 1:
         dist.barrier()
@@ -229,16 +348,13 @@ def run_ours(args):
     wb = args.weights == "bf16"
     dec = gpt.GptDecoder(path, device=local, weight_dtype=1 if wb else 0)
     info = dec.info()
-    prefix = make_prefix(dec.prepare, 1002 + rank)
-    rows = prefix.shape[0]
-    opts = gpt.gen_opts(seed=1234 + rank, temperature=0.8, top_k=30, top_p=0.8, repetition_penalty=10.0,
-                        rng=gpt.RNG_PHILOX)
+    wl = build_workload(args.config, gpt, dec, rank, world)
+    if args.codes and wl["kind"] in ("single", "batch", "beam"):
+        wl["codes"] = [args.codes] * len(wl["codes"])
+    kind = wl["kind"]
+    prefixes, opts, codes = wl["prefixes"], wl["opts"], wl["codes"]
     stream = torch.cuda.ExternalStream(dec.stream, device=local)
-    d_prefix = torch.from_numpy(prefix).to(f"cuda:{local}")
-    n_codes = args.codes
-    d_codes = torch.zeros(n_codes, dtype=torch.int32, device=f"cuda:{local}")
-    d_info = torch.zeros(4, dtype=torch.int32, device=f"cuda:{local}")
-    torch.cuda.synchronize()
+    dev = f"cuda:{local}"
 
     def barrier():
         torch.cuda.synchronize()
@@ -248,70 +364,115 @@ def run_ours(args):
     def max_over_ranks(x):
         if world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    def one_step(ev=None):
-        if ev:
-            ev[0].record(stream)
-        dec.prefill_async(d_prefix.data_ptr(), rows)
-        if ev:
-            ev[1].record(stream)
-        dec.decode_async(opts, n_codes, d_codes.data_ptr(), d_info.data_ptr())
-        if ev:
-            ev[2].record(stream)
+    # the public call of this workload (host buffers)
+    def public_call():
+        if kind == "single":
+            return [dec.generate(prefixes[0], opts[0], codes[0])]
+        if kind == "beam":
+            return [dec.generate(prefixes[0], opts[0], codes[0])]
+        if kind == "batch":
+            return dec.generate_batch(prefixes, opts, codes[0])
+        return dec.serve(prefixes, opts, codes, max_rows=args.rows)
 
-    # ---- device-resident arm (value)
-    for _ in range(args.warmup):
-        one_step()
-    dec.sync()
+    tokens_per_step = sum(codes)
+    fwd_steps, decode_ms, prefill_ms = [], [], []
     smi = ClockSampler(gpu_smi_id(local))
-    smi.start()
-    time.sleep(0.3)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    launches0 = dec.launch_count
-    start.record(stream)
-    for k in range(args.steps):
-        one_step(evs[k])
-    end.record(stream)
-    dec.sync()
-    barrier()
-    launches = dec.launch_count - launches0
+    if kind == "single":
+        # device-resident arm: prefix in HBM, prefill_async + decode_async, CUDA events on the library's stream
+        d_prefix = torch.from_numpy(prefixes[0]).to(dev)
+        rows = prefixes[0].shape[0]
+        d_codes = torch.zeros(codes[0], dtype=torch.int32, device=dev)
+        d_info = torch.zeros(4, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+
+        def one_step(ev=None):
+            if ev:
+                ev[0].record(stream)
+            dec.prefill_async(d_prefix.data_ptr(), rows)
+            if ev:
+                ev[1].record(stream)
+            dec.decode_async(opts[0], codes[0], d_codes.data_ptr(), d_info.data_ptr())
+            if ev:
+                ev[2].record(stream)
+
+        for _ in range(args.warmup):
+            one_step()
+        dec.sync()
+        smi.start()
+        time.sleep(0.3)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        launches0 = dec.launch_count
+        start.record(stream)
+        for k in range(args.steps):
+            one_step(evs[k])
+        end.record(stream)
+        dec.sync()
+        barrier()
+        launches = dec.launch_count - launches0
+        elapsed_ms = start.elapsed_time(end)
+        decode_ms = [e[1].elapsed_time(e[2]) for e in evs]
+        prefill_ms = [e[0].elapsed_time(e[1]) for e in evs]
+        fwd_steps = [int(d_info.cpu().numpy()[3])] * args.steps
+        kernel = "k_decode (persistent, batch 1)"
+    else:
+        for _ in range(args.warmup):
+            public_call()
+        smi.start()
+        time.sleep(0.3)
+        barrier()
+        launches0 = dec.launch_count
+        elapsed_ms = 0.0
+        for _ in range(args.steps):
+            public_call()
+            t = dec.last_timing()
+            decode_ms.append(t.decode_ms)
+            prefill_ms.append(t.prefill_ms)
+            fwd_steps.append(int(t.forward_steps))
+            elapsed_ms += t.prefill_ms + t.decode_ms
+        barrier()
+        launches = dec.launch_count - launches0
+        kernel = "k_bdecode (persistent, batched rows)"
     clocks = smi.stop()
-    elapsed_ms = start.elapsed_time(end)
-    decode_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    prefill_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    info_h = d_info.cpu().numpy()
-    fwd = int(info_h[3])
-    replicas = importlib.import_module("index-tts-25-metal_b200.replicas")
-    agg = replicas.aggregate(args.steps * n_codes, elapsed_ms / 1000.0, device=f"cuda:{local}")
-    elapsed_max = 1000.0 * agg["seconds"]
-    value = agg["value"]  # all ranks' codes / the slowest rank's device time
+    agg = replicas.aggregate(args.steps * tokens_per_step, elapsed_ms / 1000.0, device=dev)
+    value = agg["value"]
 
     # ---- public API with host buffers (e2e)
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        r = dec.generate(prefix, opts, n_codes)
+        res = public_call()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    assert len(r.codes) == n_codes
-    e2e_value = world * args.steps * n_codes / e2e_s
+    got = [len(r.codes) for r in res]
+    assert got == list(codes[:len(got)]) or kind == "beam", (got, codes)
+    total_tokens = args.steps * tokens_per_step
+    if world > 1:
+        t = torch.tensor([float(total_tokens)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_tokens = float(t.item())
+    e2e_value = total_tokens / e2e_s
 
+    # ---- roofline of the decode: weights once per forward step + K/V per row
     pk, pk_kind = peaks()
-    alg = decode_bytes(info.stream_bytes, info.layers, rows, fwd)
+    L = info.layers
+    if kind == "beam":
+        rows = prefixes[0].shape[0]
+        kv = sum(3 * KV_ROW_BYTES * L * (rows + i + 1) for i in range(fwd_steps[-1]))
+    else:
+        kv = sum(kv_read_bytes(L, p.shape[0], c - 1) for p, c in zip(prefixes, codes))
+    alg = fwd_steps[-1] * info.stream_bytes + kv
     avg_decode_s = statistics.mean(decode_ms) / 1000.0
     achieved = alg / avg_decode_s / 1e9
     peak_gbs = float(pk["hbm_gbs"])
-    # DRAM traffic of the decode kernel: the ratio of DRAM bytes (ncu,
-    # dram__bytes_read.sum + dram__bytes_write.sum) to algorithmic bytes of a
-    # small captured launch, applied to this launch's algorithmic bytes
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tpath) and not wb:  # the captured ratio is the fp32 kernel's
+    if kind == "single" and os.path.exists(tpath) and not wb:  # the captured ratio is the fp32 batch-1 kernel's
         with open(tpath) as f:
             tj = json.load(f)
         if tj.get("capture_dram_bytes") and tj.get("capture_algorithmic_bytes"):
@@ -319,31 +480,32 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, kind, cores, sample = cpu_reference_sample(prefix, args.cpu_tokens)
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+        cpu = cpu_baseline(prefixes[0], args)
 
     if rank == 0:
+        h2d = int(sum(p.nbytes for p in prefixes))
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * agg["seconds"] / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, seeded conditioning latents and text ids)",
-            "config": {"workload": "configs[1]: sampled decode (T 0.8, top-k 30, top-p 0.8, rp 10, Philox "
-                                   f"seed 1234), prefix 32 latents + 200 text tokens, {n_codes} codes, batch 1",
+            "config": {"workload": wl["desc"], "config": args.config,
                        "model": "UnifiedVoice GPT 24L d1280 H20 FFN5120 fp32 random-init (seed 42)",
                        "weights": "bf16 matrices (fp32 LN, bias, KV, accumulation)" if wb else "fp32",
-                       "global_batch": world, "prefix_rows": rows, "codes_per_request": n_codes,
-                       "parallelism": f"replicas x{world} (one request per GPU, no collective)",
-                       "l2": "inputs larger than L2: each forward step streams 1.93 GB of weights (L2 126 MB)",
-                       "decode_mode": "persistent cooperative kernel"},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(prefix.nbytes),
-                    "d2h_bytes_per_step": int(n_codes * 4 + 48)},
+                       "global_batch": world * len(prefixes), "prefix_rows": [int(p.shape[0]) for p in prefixes][:16],
+                       "codes_per_request": codes[:16], "requests_per_rank": len(prefixes),
+                       "parallelism": f"replicas x{world} (independent requests per GPU, no collective)",
+                       "l2": "inputs larger than L2: each forward step streams the weights (1.93 GB fp32) "
+                             "through a 126 MB L2",
+                       "rows_in_flight": args.rows if kind == "serve" else len(prefixes)},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": int(4 * tokens_per_step + 48 * len(prefixes))},
             "gpu_launches": int(launches),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "traffic": traffic,
-                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": "k_decode_persistent",
+                         "peak_source": f"{pk_kind} hbm_gbs", "kernel": kernel,
                          "algorithmic_bytes_per_launch": alg, "avg_launch_ms": 1000 * avg_decode_s,
-                         "forward_steps_per_launch": fwd},
+                         "forward_steps_per_launch": fwd_steps[-1]},
             "prefill_ms": statistics.mean(prefill_ms),
             "clocks": clocks,
         }
@@ -361,13 +523,17 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["0", "1", "2", "2beam", "3", "serving"], default="1",
+                    help="BASELINE.json workload (1 = the headline)")
+    ap.add_argument("--rows", type=int, default=16, help="rows in flight for --config serving")
     ap.add_argument("--cpu-tokens", type=int, default=48)
+    ap.add_argument("--cpu-tokens-1t", type=int, default=6)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--weights", choices=["f32", "bf16"], default="f32",
                     help="weight storage of the decoder (the headline is f32; bf16 is the optional weight path)")
-    ap.add_argument("--codes", type=int, default=N_CODES,
-                    help="codes per request (1024 is the benchmark; smaller values are for profiler captures)")
+    ap.add_argument("--codes", type=int, default=0,
+                    help="override codes per request (profiler captures only; 0 = the config's own)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -148,6 +148,21 @@ int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const*
                             const itts_gen_opts* opts, uint32_t max_tokens, uint32_t* codes, uint32_t* n_codes,
                             int* stopped);
 
+/* ---- continuous batching --------------------------------------------------
+ * The serving loop: request i (prefix prefixes[i], options opts[i], at most
+ * max_tokens[i] codes into codes[i]) is decoded as generate would decode it
+ * alone, with up to max_rows (<= 16) requests in flight on the device: each
+ * batched step reads the weights once for every row in flight, and a row
+ * whose request finished takes the next request (in the given order) at the
+ * next host sync point.  n_codes[i] / stopped[i] as in itts_gpt_generate.
+ * Requests with num_beams > 1 are rejected.  No single call of the
+ * reference corresponds: its server runs GptDecoder::generate once per
+ * request (src/server.cpp:41-47, gpt_sampling.cpp:168-189).  Afterwards the
+ * context holds no prefill. */
+int itts_gpt_serve(itts_gpt_ctx* ctx, size_t n, const float* const* prefixes, const size_t* n_floats,
+                   const itts_gen_opts* opts, const uint32_t* max_tokens, uint32_t max_rows, uint32_t* const* codes,
+                   uint32_t* n_codes, int* stopped);
+
 /* ---- GptDecoder::checkpoint / restore / cached_tokens (gpt.cpp:86-87) ----- */
 int itts_gpt_checkpoint(itts_gpt_ctx* ctx, itts_gpt_state** out);
 int itts_gpt_restore(itts_gpt_ctx* ctx, const itts_gpt_state* state);

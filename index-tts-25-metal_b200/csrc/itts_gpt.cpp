@@ -113,7 +113,7 @@ struct itts_gpt_ctx {
     float* d_btmp = nullptr;         // beam search: [kMaxBatch][8448] log-softmax scratch
     uint32_t* d_bhist = nullptr;     // beam search: [kMaxBatch][kCap + 2] histories
     itts::BatchState* h_bstate = nullptr;  // pinned
-    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};  // generate timing: start, prefill done, decode done
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};  // generate timing: start, prefill done, decode done; serve start
     itts_gpt_timing timing{};        // accumulated over the last generate / generate_batch call
     bool pending = false;           // an async decode has not been synced yet
     uint32_t* pending_info = nullptr;
@@ -617,9 +617,10 @@ void batch_forward(itts_gpt_ctx* c, const itts::BatchArgs& a) {
        "batched forward launch");
 }
 
-// `iters` draws of every active row, each followed by a forward step while a
-// row is active (persistent kernel; layered mode: one sampler launch and one
-// forward per iteration).
+// `iters` iterations of: a draw of every active row, then a forward step of
+// the rows still active (persistent kernel; layered mode: one sampler launch
+// and one forward launch sequence, whose kernels return at once when no row
+// is active).
 void batch_generate(itts_gpt_ctx* c, const itts::BatchArgs& a, uint32_t iters) {
     if (c->mode == 0) {
         reset_ctl(c);
@@ -632,7 +633,6 @@ void batch_generate(itts_gpt_ctx* c, const itts::BatchArgs& a, uint32_t iters) {
     for (uint32_t i = 0; i < iters; ++i) {
         ck(itts::launch_batch_sample(a, c->stream), "batched sampler launch");
         ++c->launches;
-        if (i + 1 == iters) break;
         batch_forward(c, a);
     }
 }
@@ -697,6 +697,101 @@ void generate_rows(itts_gpt_ctx* c, size_t M, const float* const* prefixes, cons
         stopped[m] = int(st.stopped[m]);
         std::memcpy(codes + m * size_t(max_tokens), out.data() + m * size_t(max_tokens), size_t(st.n_codes[m]) * 4);
     }
+    c->cached = 0;  // the context's own cache no longer follows a prefill
+    c->have_prefill = false;
+}
+
+// Continuous batching: requests (gpt_sampling.cpp:168-189 each) decoded with
+// up to R rows in flight.  The host meets the device at sync points: finished
+// rows hand their codes back and the next requests are prefilled into the
+// free rows (each row its own KV arena, start step and code limit); then the
+// batched kernel runs until the first row reaches its limit (at most
+// kServeChunk steps, so a row that ends on the stop code waits at most that
+// long for a successor).
+constexpr uint32_t kServeChunk = 64;
+
+void serve_rows(itts_gpt_ctx* c, size_t n, const float* const* prefixes, const size_t* n_floats,
+                const itts::SampleOpts* o, const uint32_t* max_tokens, uint32_t max_rows, uint32_t* const* codes,
+                uint32_t* n_codes, int* stopped) {
+    using namespace itts;
+    const uint32_t R = uint32_t(std::min<size_t>({size_t(max_rows), n, size_t(kMaxBatch)}));
+    ensure_batch(c, R);
+    reset_ctl(c);
+    ck(cudaMemsetAsync(c->bargs.head_cnt, 0, size_t(24) * kMaxBatch * kH * 4, c->stream), "counter reset");
+    BatchState& st = *c->h_bstate;
+    ck(cudaStreamSynchronize(c->stream), "serve start");
+    std::memset(&st, 0, sizeof st);
+    std::vector<long> row_req(R, -1);
+    std::vector<SampleOpts> ro(kMaxBatch, o[0]);
+    size_t next = 0;
+    uint32_t forwards = 0;
+    mark(c, 3);
+    float prefill_ms = 0.f;
+    cudaEvent_t e0 = c->ev[0], e1 = c->ev[1];
+    for (;;) {
+        // admit requests into free rows
+        bool admitted = false;
+        for (uint32_t m = 0; m < R && next < n; ++m) {
+            if (row_req[m] >= 0) continue;
+            if (!admitted) ck(cudaEventRecord(e0, c->stream), "event record");
+            admitted = true;
+            const size_t q = next++;
+            batch_prefill(c, prefixes[q], n_floats[q], m, m);
+            st.s0[m] = uint32_t(n_floats[q] / kW);
+            st.arena[m] = m;
+            st.base[m] = st.step;
+            st.maxc[m] = max_tokens[q];
+            st.n_codes[m] = 0;
+            st.stopped[m] = 0;
+            st.active |= 1u << m;
+            ro[m] = o[q];
+            uint32_t seen[kSeenWords] = {};
+            for (uint32_t t : {1u, 8192u}) seen[t >> 5] |= 1u << (t & 31);
+            ck(cudaMemcpyAsync(c->bargs.seen + size_t(m) * kSeenWords, seen, sizeof seen, cudaMemcpyHostToDevice,
+                               c->stream),
+               "seen upload");
+            row_req[m] = long(q);
+        }
+        if (admitted) {
+            ck(cudaEventRecord(e1, c->stream), "event record");
+            ck(cudaEventSynchronize(e1), "prefill");
+            float ms = 0.f;
+            ck(cudaEventElapsedTime(&ms, e0, e1), "event time");
+            prefill_ms += ms;
+        }
+        if (!st.active) break;
+        uint32_t iters = kServeChunk;
+        for (uint32_t m = 0; m < R; ++m)
+            if ((st.active >> m) & 1u) iters = std::min(iters, st.maxc[m] - (st.step - st.base[m]));
+        put_state(c);
+        BatchArgs a = batch_args(c, R, ro.data(), true);
+        a.codes_stride = kCap;
+        batch_generate(c, a, iters);
+        forwards += iters;
+        ck(cudaMemcpyAsync(c->h_bstate, c->bargs.st, sizeof(BatchState), cudaMemcpyDeviceToHost, c->stream),
+           "batch state read");
+        check_status(c);
+        // hand finished rows back
+        for (uint32_t m = 0; m < R; ++m) {
+            if (row_req[m] < 0 || ((st.active >> m) & 1u)) continue;
+            const size_t q = size_t(row_req[m]);
+            n_codes[q] = st.n_codes[m];
+            stopped[q] = int(st.stopped[m]);
+            if (st.n_codes[m])
+                ck(cudaMemcpy(codes[q], c->bargs.codes + size_t(m) * kCap, size_t(st.n_codes[m]) * 4,
+                              cudaMemcpyDeviceToHost),
+                   "codes read");
+            row_req[m] = -1;
+        }
+    }
+    mark(c, 2);
+    ck(cudaStreamSynchronize(c->stream), "serve end");
+    float total = 0.f;
+    ck(cudaEventElapsedTime(&total, c->ev[3], c->ev[2]), "event time");
+    c->timing.prefill_ms += prefill_ms;
+    c->timing.decode_ms += total - prefill_ms;
+    c->timing.forward_steps += forwards;
+    c->timing.rows = std::max(c->timing.rows, R);
     c->cached = 0;  // the context's own cache no longer follows a prefill
     c->have_prefill = false;
 }
@@ -1164,6 +1259,29 @@ int itts_gpt_generate_batch(itts_gpt_ctx* ctx, size_t batch, const float* const*
                 std::memcpy(codes + i * size_t(max_tokens), cc.data() + k * size_t(max_tokens), size_t(nc[k]) * 4);
             }
         }
+    });
+}
+
+int itts_gpt_serve(itts_gpt_ctx* ctx, size_t n, const float* const* prefixes, const size_t* n_floats,
+                   const itts_gen_opts* opts, const uint32_t* max_tokens, uint32_t max_rows, uint32_t* const* codes,
+                   uint32_t* n_codes, int* stopped) {
+    if (!ctx) return ITTS_ERR_INVALID_ARGUMENT;
+    return guard(ctx, [&] {
+        finish_pending(ctx);
+        if (n == 0) return;
+        if (!prefixes || !n_floats || !opts || !max_tokens || !codes || !n_codes || !stopped)
+            invalid("null serve argument");
+        if (max_rows == 0) invalid("max_rows must be at least 1");
+        std::vector<itts::SampleOpts> o(n);
+        for (size_t i = 0; i < n; ++i) {  // every request is checked before any runs
+            if (!prefixes[i] || !codes[i]) invalid("null prefix or code buffer in serve");
+            validate_prefix(n_floats[i]);
+            validate_capacity(ctx, n_floats[i] / kW, max_tokens[i]);
+            o[i] = configure(opts[i], nullptr);
+            if (o[i].num_beams > 1) invalid("serve decodes requests without beams");
+        }
+        ctx->timing = itts_gpt_timing{};
+        serve_rows(ctx, n, prefixes, n_floats, o.data(), max_tokens, max_rows, codes, n_codes, stopped);
     });
 }
 

@@ -79,6 +79,7 @@ SIGNATURES = {
     "itts_gpt_generate": (C.c_int, [_P, _P, C.c_size_t, C.POINTER(GenOpts), C.c_uint32, _P,
                                     C.POINTER(C.c_uint32), C.POINTER(C.c_int)]),
     "itts_gpt_generate_batch": (C.c_int, [_P, C.c_size_t, _P, _P, _P, C.c_uint32, _P, _P, _P]),
+    "itts_gpt_serve": (C.c_int, [_P, C.c_size_t, _P, _P, _P, _P, C.c_uint32, _P, _P, _P]),
     "itts_gpt_checkpoint": (C.c_int, [_P, C.POINTER(_P)]),
     "itts_gpt_restore": (C.c_int, [_P, _P]),
     "itts_gpt_state_free": (None, [_P]),
@@ -284,6 +285,29 @@ class GptDecoder:
                                                       C.cast(opts, C.c_void_p), max_tokens, _ptr(codes), _ptr(n),
                                                       _ptr(st)))
         return [GenerationResult(codes[i, :n[i]].copy(), bool(st[i])) for i in range(b)]
+
+    def serve(self, prefixes, options, max_tokens, max_rows: int = 16) -> list:
+        """Continuous batching (itts_gpt_serve): request i decoded as
+        generate(prefixes[i], options[i], max_tokens[i]) would decode it, with
+        up to max_rows requests in flight; one GenerationResult per request."""
+        ps = [_f32(p).ravel() for p in prefixes]
+        b = len(ps)
+        if len(options) != b or len(max_tokens) != b:
+            raise ValueError("one GenOpts and one max_tokens per prefix")
+        if b == 0:
+            return []
+        ptrs = (C.c_void_p * b)(*[p.ctypes.data for p in ps])
+        sizes = (C.c_size_t * b)(*[p.size for p in ps])
+        opts = (GenOpts * b)(*options)
+        mx = np.ascontiguousarray(max_tokens, np.uint32)
+        bufs = [np.zeros(max(1, int(m)), np.uint32) for m in mx]
+        cptrs = (C.c_void_p * b)(*[x.ctypes.data for x in bufs])
+        n = np.zeros(b, np.uint32)
+        st = np.zeros(b, np.int32)
+        self._check(self._lib.itts_gpt_serve(self._h, b, C.cast(ptrs, C.c_void_p), C.cast(sizes, C.c_void_p),
+                                             C.cast(opts, C.c_void_p), _ptr(mx), max_rows,
+                                             C.cast(cptrs, C.c_void_p), _ptr(n), _ptr(st)))
+        return [GenerationResult(bufs[i][:n[i]].copy(), bool(st[i])) for i in range(b)]
 
     def checkpoint(self) -> GptState:
         s = C.c_void_p()

@@ -106,3 +106,49 @@ def test_beam_search_matches_oracle(dec_masked, port_masked, gpt_mod, oracle_mod
     e, st = port_masked.generate(prefix, oracle_mod.make_opts(**kw), n)
     np.testing.assert_array_equal(r.codes, e)
     assert r.stopped == st
+
+
+def test_serve_matches_generate_per_request(dec_masked, port_masked, gpt_mod, oracle_mod):
+    """itts_gpt_serve (continuous batching): 11 requests of different prefix
+    lengths and code limits through 4 rows; each request's codes equal a
+    batch-1 generate of it alone, and the oracle's for a few."""
+    lengths = [20, 160, 7, 90, 240, 33, 5, 120, 64, 11, 180]
+    limits = [30, 12, 45, 8, 25, 40, 17, 9, 33, 21, 5]
+    prefixes = ragged_prefixes(77, lengths)
+    kws = [OPTION_MIX[(i + 3) % len(OPTION_MIX)] for i in range(len(lengths))]
+    res = dec_masked.serve(prefixes, [gpt_mod.gen_opts(**k) for k in kws], limits, max_rows=4)
+    t = dec_masked.last_timing()
+    assert t.rows == 4 and t.forward_steps > 0 and t.decode_ms > 0 and t.prefill_ms > 0
+    assert len(res) == len(lengths)
+    for i, (p, k, n, r) in enumerate(zip(prefixes, kws, limits, res)):
+        single = dec_masked.generate(p, gpt_mod.gen_opts(**k), n)
+        np.testing.assert_array_equal(r.codes, single.codes, err_msg=f"request {i}")
+        assert len(r.codes) == n and not r.stopped
+        if i < 2:
+            e, _ = port_masked.generate(p, oracle_mod.make_opts(**k), n)
+            np.testing.assert_array_equal(r.codes, e, err_msg=f"request {i} vs oracle")
+
+
+def test_serve_layered_mode_and_stop(gpt_mod, shallow_bundle, dec_masked):
+    """Layered mode gives the same codes; a request that ends on the stop code
+    frees its row for the next request."""
+    prefixes = ragged_prefixes(78, [15, 40, 9, 70, 22])
+    opts = [gpt_mod.gen_opts(seed=40 + i) for i in range(5)]
+    limits = [12, 20, 7, 16, 10]
+    a = dec_masked.serve(prefixes, opts, limits, max_rows=2)
+    dec_masked.set_decode_mode(1)
+    try:
+        b = dec_masked.serve(prefixes, opts, limits, max_rows=2)
+    finally:
+        dec_masked.set_decode_mode(0)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x.codes, y.codes)
+    # unmasked bundle: generate decides where each request stops
+    with gpt_mod.GptDecoder(shallow_bundle) as dec:
+        ps = ragged_prefixes(79, [10, 30, 50, 8])
+        os_ = [gpt_mod.gen_opts(seed=50 + i, temperature=1.5, top_k=0, top_p=1.0) for i in range(4)]
+        res = dec.serve(ps, os_, [60] * 4, max_rows=3)
+        for p, o, r in zip(ps, os_, res):
+            single = dec.generate(p, o, 60)
+            np.testing.assert_array_equal(r.codes, single.codes)
+            assert r.stopped == single.stopped
