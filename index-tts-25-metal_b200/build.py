@@ -72,7 +72,28 @@ def build(verbose: bool = False, force: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    build_op_server(force)
     return LIB
+
+
+SERVER_SRC = os.path.join(HERE, "host", "gpt_op_server.cpp")
+SERVER = os.path.join(HERE, "itts_gpt_op_server")
+
+
+def build_op_server(force: bool = False) -> str:
+    """The line-protocol `gpt` op server (host/gpt_op_server.cpp), linked
+    against the library next to it."""
+    deps = [SERVER_SRC, LIB, os.path.join(HERE, "host", "gpt_decoder.hpp"), os.path.join(CSRC, "mit2_bundle.hpp"),
+            os.path.join(INCLUDE, "itts_gpt.h")]
+    if not force and os.path.exists(SERVER) and all(os.path.getmtime(d) <= os.path.getmtime(SERVER) for d in deps):
+        return SERVER
+    cmd = [HOST_CXX, "-std=c++17", "-O2", "-Wall", "-I", INCLUDE, "-I", os.path.join(HERE, "host"), "-I", CSRC,
+           "-I", os.path.join(CUDA, "include"), SERVER_SRC, "-L", HERE, "-litts_gpt_b200", "-Wl,-rpath,$ORIGIN",
+           "-o", SERVER]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"op server build failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return SERVER
 
 
 if __name__ == "__main__":
