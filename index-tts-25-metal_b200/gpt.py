@@ -96,6 +96,11 @@ SIGNATURES = {
     "itts_gpt_wait_probe": (C.c_int, [_P]),
     "itts_gpt_apply_processors_noalloc": (C.c_int, [C.c_int, _P, C.c_size_t, _P, C.c_size_t, C.POINTER(GenOpts),
                                                     _P]),
+    # include/itts_codec.h
+    "itts_codec_create": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_P)]),
+    "itts_codec_destroy": (None, [_P]),
+    "itts_codec_last_error": (C.c_char_p, [_P]),
+    "itts_codec_decode": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t]),
 }
 
 _lib = None
@@ -354,3 +359,42 @@ def apply_processors_noalloc(logits, history, options: GenOpts, device: int = 0)
     if rc != OK:
         _raise(rc, lib.itts_gpt_last_error(None).decode())
     return out
+
+
+class SemanticCodec:
+    """The decode half of the reference's itts25::EnhancedCodec
+    (include/itts25/codec.hpp) over include/itts_codec.h: semantic codes ->
+    [2n, 1024] features."""
+
+    def __init__(self, bundle_dir: str, device: int = 0):
+        self._lib = load_library()
+        h = C.c_void_p()
+        rc = self._lib.itts_codec_create(bundle_dir.encode(), device, C.byref(h))
+        if rc != OK:
+            _raise(rc, self._lib.itts_codec_last_error(None).decode())
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.itts_codec_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def decode(self, codes) -> np.ndarray:
+        c = _u32(codes)
+        out = np.empty((max(1, 2 * c.size), 1024), np.float32)
+        rc = self._lib.itts_codec_decode(self._h, _ptr(c), c.size, _ptr(out), out.size)
+        if rc != OK:
+            _raise(rc, self._lib.itts_codec_last_error(self._h).decode())
+        return out[:2 * c.size]

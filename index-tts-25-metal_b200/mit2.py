@@ -97,6 +97,86 @@ def _tensor_values(seed: int, index: int, shape, kind: str, std: float):
     return v
 
 
+def codec_tensor_specs():
+    """Ordered (name, shape, kind) list of the IndexTTS 2.5 semantic codec
+    (src/codec.cpp:6-22 shape checks and the tensors decode/encode read):
+    a factorized quantizer (codebook 8192 x 8, 8 <-> 1024 projections), a
+    ConvNeXt "vocos" encoder and decoder (k=7 embedding conv 1024 -> 384,
+    12 blocks of depthwise k=7 conv, LayerNorm, 384 -> 2048 -> 384 pointwise
+    linears and a layer scale, final LayerNorm, linear 384 -> 1024), and the
+    stride-2 down / k=3 up convolutions."""
+    q = "codec.quantizer.quantizers.0"
+    specs = [
+        ("codec.down.weight", (1024, 1024, 3), "mat"), ("codec.down.bias", (1024,), "bias"),
+        ("codec.up.weight", (1024, 1024, 3), "mat"), ("codec.up.bias", (1024,), "bias"),
+        (f"{q}.codebook.weight", (8192, 8), "unit"),
+        (f"{q}.in_project.weight", (8, 1024), "mat"), (f"{q}.in_project.bias", (8,), "bias"),
+        (f"{q}.out_project.weight", (1024, 8), "mat"), (f"{q}.out_project.bias", (1024,), "bias"),
+    ]
+    for block in ("encoder", "decoder"):
+        p = f"codec.{block}.0"
+        specs += [(f"{p}.embed.weight", (384, 1024, 7), "mat"), (f"{p}.embed.bias", (384,), "bias"),
+                  (f"{p}.norm.weight", (384,), "ln_w"), (f"{p}.norm.bias", (384,), "ln_b")]
+        for i in range(12):
+            c = f"{p}.convnext.{i}"
+            specs += [(f"{c}.dwconv.weight", (384, 1, 7), "mat"), (f"{c}.dwconv.bias", (384,), "bias"),
+                      (f"{c}.norm.weight", (384,), "ln_w"), (f"{c}.norm.bias", (384,), "ln_b"),
+                      (f"{c}.pwconv1.weight", (2048, 384), "mat"), (f"{c}.pwconv1.bias", (2048,), "bias"),
+                      (f"{c}.pwconv2.weight", (384, 2048), "mat"), (f"{c}.pwconv2.bias", (384,), "bias"),
+                      (f"{c}.gamma", (384,), "ln_w")]
+        specs += [(f"{p}.final_layer_norm.weight", (384,), "ln_w"), (f"{p}.final_layer_norm.bias", (384,), "ln_b"),
+                  (f"codec.{block}.1.weight", (1024, 384), "mat"), (f"codec.{block}.1.bias", (1024,), "bias")]
+    return specs
+
+
+def write_synthetic_codec_bundle(path: str, *, seed: int = 43, std: float = 0.02, alignment: int = 256,
+                                 reuse: bool = True) -> str:
+    """Random-init semantic-codec bundle (target index-tts2.5) at ``path``;
+    returns the SHA-256 of ``weights.bin`` (an existing complete bundle with
+    the same arguments is reused).  Matrices N(0, std); LayerNorm weights and
+    layer scales 1 + N(0, std); codebook rows N(0, 1)."""
+    args = dict(kind="codec", seed=seed, std=std, alignment=alignment)
+    os.makedirs(path, exist_ok=True)
+    marker = os.path.join(path, ".complete")
+    if reuse and bundle_complete(path):
+        with open(marker) as f:
+            rec = json.load(f)
+        if rec.get("args") == args:
+            return rec["sha256"]
+    if os.path.exists(marker):
+        os.remove(marker)
+    records, offset, h = [], alignment, hashlib.sha256()
+    with open(os.path.join(path, "weights.bin"), "wb") as f:
+        header = b"MIT2" + struct.pack("<II", 1, alignment)
+        header += b"\0" * (alignment - len(header))
+        f.write(header)
+        h.update(header)
+        for idx, (name, shape, kind) in enumerate(codec_tensor_specs()):
+            v = _tensor_values(seed, idx, shape, "mat", 1.0 if kind == "unit" else std)
+            if kind == "ln_w":
+                v += np.float32(1.0)
+            raw = v.tobytes()
+            f.write(raw)
+            h.update(raw)
+            records.append({"name": name, "shape": list(shape), "dtype": "f32", "offset": offset,
+                            "nbytes": len(raw), "component": "codec"})
+            offset += len(raw)
+            pad = (-offset) % alignment
+            if pad:
+                f.write(b"\0" * pad)
+                h.update(b"\0" * pad)
+                offset += pad
+    manifest = {"format": "MIT2", "version": 1, "alignment": alignment, "endianness": "little",
+                "target": "index-tts2.5", "weights_file": "weights.bin",
+                "synthetic": {"seed": seed, "std": std, "init": "normal", "component": "codec"}, "tensors": records}
+    with open(os.path.join(path, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=0)
+    digest = h.hexdigest()
+    with open(marker, "w") as f:
+        json.dump({"args": args, "sha256": digest}, f)
+    return digest
+
+
 def bundle_complete(path: str) -> bool:
     return os.path.exists(os.path.join(path, "manifest.json")) and \
         os.path.exists(os.path.join(path, ".complete"))

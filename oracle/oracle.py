@@ -228,6 +228,42 @@ class RefOracle(_Oracle):
         return os.path.exists(cls.so)
 
 
+class RefCodec:
+    """The reference's own EnhancedCodec (src/codec.cpp) on the CPU shim
+    (oracle/_ref/libitts_ref.so, codec_shim.cpp): decode of semantic codes."""
+    _lib = None
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            lib = C.CDLL(REF_SO)
+            lib.ref_codec_last_error.restype = C.c_char_p
+            lib.ref_codec_load.restype = C.c_void_p
+            lib.ref_codec_load.argtypes = [C.c_char_p]
+            lib.ref_codec_free.argtypes = [C.c_void_p]
+            lib.ref_codec_decode.argtypes = [C.c_void_p, _U, C.c_size_t, _F, C.c_size_t]
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, bundle_dir: str):
+        self.h = self.lib().ref_codec_load(bundle_dir.encode())
+        if not self.h:
+            raise OracleError(-2, self.lib().ref_codec_last_error().decode())
+
+    def decode(self, codes) -> np.ndarray:
+        c = np.ascontiguousarray(codes, np.uint32)
+        out = np.empty(max(1, 2 * c.size) * 1024, np.float32)
+        rc = self.lib().ref_codec_decode(self.h, c, c.size, out, out.size)
+        if rc != 0:
+            raise OracleError(rc, self.lib().ref_codec_last_error().decode())
+        return out[:2 * c.size * 1024].reshape(2 * c.size, 1024)
+
+    def close(self):
+        if self.h:
+            self.lib().ref_codec_free(self.h)
+            self.h = None
+
+
 def compare(actual, expected, tol=1e-4, rms_tol=1e-5):
     """The reference comparator (src/main.cpp:19-30): finite check, max_abs,
     mean_abs and RMSE; passes when max_abs < tol and rmse < rms_tol."""

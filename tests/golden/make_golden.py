@@ -28,6 +28,9 @@ Fixtures (all inputs seeded):
                      emotion-conditioning rows + 400 text ids + start row = 451
                      rows; prefill logits, two teacher-forced step logits and 128
                      SplitMix64 sampled codes (seed 1234).
+  codec.npz          the semantic codec's decode (src/codec.cpp:50-69) on a
+                     random-init codec bundle (seed 43): codes of 1 and 17
+                     tokens and their [2n, 1024] features.
   gpt_config1_philox.npz  configs[1] with the Philox4x32-10 stream (the
                      benchmark's mode, seed 1234): 1024 sampled codes from the
                      oracle port (the reference has only SplitMix64; the port
@@ -203,6 +206,19 @@ def make_config1_philox(path, sha, out, n_codes):
     print("wrote", out)
 
 
+def make_codec(out):
+    path = os.path.join(CACHE, "codec_s43")
+    sha = mit2.write_synthetic_codec_bundle(path, seed=43)
+    ref = O.RefCodec(path)
+    d = {"bundle_seed": 43, "bundle_sha256": sha}
+    for name, n in (("one", 1), ("short", 17)):
+        codes = np.random.default_rng(4300 + n).integers(0, 8192, n).astype(np.uint32)
+        d[f"{name}.codes"] = codes
+        d[f"{name}.features"] = ref.decode(codes)
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
 PROCESSOR_CASES = {
     # name: [temperature, top_k, top_p, repetition_penalty, num_beams]
     "standard": [0.8, 30, 0.8, 10.0, 1],
@@ -235,7 +251,7 @@ def make_processors(out):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", choices=["full", "long", "processors", "config2_beam", "config2_batch", "config3",
-                                       "config1_philox"], default=None)
+                                       "config1_philox", "codec"], default=None)
     ap.add_argument("--config2-codes", type=int, default=600)
     ap.add_argument("--long-codes", type=int, default=1024)
     a = ap.parse_args()
@@ -249,6 +265,8 @@ def main():
     if a.only in (None, "long"):
         path, sha = bundle(42, 24, True)
         make_long(path, sha, os.path.join(HERE, "gpt_long.npz"), a.long_codes)
+    if a.only in (None, "codec"):
+        make_codec(os.path.join(HERE, "codec.npz"))
     if a.only in (None, "config3"):
         path, sha = bundle(42, 24, True)
         make_config3(path, sha, os.path.join(HERE, "gpt_config3.npz"))
