@@ -440,6 +440,20 @@ def run_ours(args):
         kernel = "k_bdecode (persistent, batched rows)"
     clocks = smi.stop()
     agg = replicas.aggregate(args.steps * tokens_per_step, elapsed_ms / 1000.0, device=dev)
+
+    # the same prefill on the CUDA-core fp32 GEMM tiles (prefill mode 1), for comparison
+    cuda_core_prefill_ms = None
+    if kind == "single" and not wb:
+        dec.set_prefill_mode(1)
+        dec.prefill_async(d_prefix.data_ptr(), rows)
+        pe = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+        for k in range(args.steps):
+            pe[2 * k].record(stream)
+            dec.prefill_async(d_prefix.data_ptr(), rows)
+            pe[2 * k + 1].record(stream)
+        dec.sync()
+        cuda_core_prefill_ms = statistics.mean(pe[2 * k].elapsed_time(pe[2 * k + 1]) for k in range(args.steps))
+        dec.set_prefill_mode(0)
     value = agg["value"]
 
     # ---- public API with host buffers (e2e)
@@ -507,6 +521,10 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": alg, "avg_launch_ms": 1000 * avg_decode_s,
                          "forward_steps_per_launch": fwd_steps[-1]},
             "prefill_ms": statistics.mean(prefill_ms),
+            "prefill": {"ms": statistics.mean(prefill_ms),
+                        "gemm": "tcgen05 TF32 hi/lo, three products (TMA-fed)" if not wb
+                        else "tcgen05 TF32 hi/lo (register-staged, bf16 weights)",
+                        "cuda_core_fp32_ms": cuda_core_prefill_ms},
             "clocks": clocks,
         }
         if cpu:

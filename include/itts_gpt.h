@@ -194,6 +194,12 @@ int itts_gpt_sync(itts_gpt_ctx* ctx);
  * barriers between phases; default); mode 1: layered decode (one launch per
  * phase, same device code).  Counters: kernel launches issued by the context. */
 int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode);
+/* Prefill GEMMs of an fp32-weight context.  mode 0 (default): tcgen05 tensor
+ * cores, operands split into two TF32 words (hi, lo) and three products per
+ * term, accumulator drained to fp32 every 128 K; mode 1: fp32 FMA tiles on the
+ * CUDA cores.  bf16-weight contexts always use the tensor cores.  Both modes
+ * replace the fp32 MPS GEMMs of the reference's prefill (gpt.cpp:88-125). */
+int itts_gpt_set_prefill_mode(itts_gpt_ctx* ctx, int mode);
 uint64_t itts_gpt_launch_count(const itts_gpt_ctx* ctx);
 
 /* Device time of the last itts_gpt_generate / itts_gpt_generate_batch call,

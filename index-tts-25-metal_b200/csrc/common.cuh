@@ -142,6 +142,13 @@ __device__ __forceinline__ void set_status(int* status, int code, int where, int
 }
 
 // tanh GELU with the clamps of mit2_gelu_f32 (kernels.metal:486-503).
+// TF32 rounding to nearest (ties away from zero) of an fp32 value: the top 19
+// bits of the word after adding half of the dropped part.  x - rn_tf32(x) is
+// exact in fp32; the pair is the hi / lo split of the tensor-core GEMMs.
+__device__ __forceinline__ float rn_tf32(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
 __device__ __forceinline__ float gelu_ref(float v) {
     if (v > 10.0f) return v;
     if (v < -10.0f) return 0.0f;

@@ -73,6 +73,8 @@ struct itts_gpt_state {
 
 struct itts_gpt_ctx {
     int device = 0, dtype = 0, sm_count = 0, mode = 0;
+    int prefill_mode = 0;           // 0: tensor-core GEMMs, 1: CUDA-core fp32 tiles (fp32 weights)
+    itts::TmaPrefill tma{};         // fp32 weights: TF32-split weights and activations of the tensor-core prefill
     cudaStream_t stream = nullptr;
     std::string err;
     uint32_t layers = 0, mel_pos_rows = 0, text_pos_rows = 0;
@@ -129,6 +131,7 @@ struct itts_gpt_ctx {
             if (p) cudaFreeHost(p);
         for (cudaEvent_t e : ev)
             if (e) cudaEventDestroy(e);
+        itts::tma_prefill_free(&tma);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -411,10 +414,16 @@ void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     }
 }
 
+// The tensor-core prefill state of an fp32 context in prefill mode 0, else null.
+itts::TmaPrefill* tma_of(itts_gpt_ctx* c) {
+    return c->dtype == ITTS_WEIGHTS_F32 && c->prefill_mode == 0 && c->tma.wsplit ? &c->tma : nullptr;
+}
+
 // prefix already in d_hidden
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
-    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x,    c->d_qkv,  c->d_att, c->d_r, c->d_ff,
-                        c->d_kv, int(rows),   c->dtype == ITTS_WEIGHTS_BF16, c->db.ctl->status};
+    itts::PrefillArgs p{&c->hw,   c->d_hidden, c->d_x,    c->d_qkv,  c->d_att,
+                        c->d_r,   c->d_ff,     c->d_kv,   int(rows), c->dtype == ITTS_WEIGHTS_BF16,
+                        c->db.ctl->status,     tma_of(c)};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     reset_ctl(c);
     itts::DecodeArgs a = decode_args(c);
@@ -587,9 +596,18 @@ void batch_prefill(itts_gpt_ctx* c, const float* prefix, size_t n_floats, uint32
     if (!prefix) invalid("prefix is null");
     const uint32_t rows = uint32_t(n_floats / kW);
     ck(cudaMemcpyAsync(c->d_hidden, prefix, n_floats * 4, cudaMemcpyHostToDevice, c->stream), "prefix upload");
-    itts::PrefillArgs p{&c->hw, c->d_hidden, c->d_x,    c->d_qkv,  c->d_att, c->d_r, c->d_ff,
-                        c->d_bkv + size_t(arena) * c->arena_floats, int(rows), c->dtype == ITTS_WEIGHTS_BF16,
-                        c->db.ctl->status};
+    itts::PrefillArgs p{&c->hw,
+                        c->d_hidden,
+                        c->d_x,
+                        c->d_qkv,
+                        c->d_att,
+                        c->d_r,
+                        c->d_ff,
+                        c->d_bkv + size_t(arena) * c->arena_floats,
+                        int(rows),
+                        c->dtype == ITTS_WEIGHTS_BF16,
+                        c->db.ctl->status,
+                        tma_of(c)};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     itts::DecodeArgs a = decode_args(c);
     a.head_src = c->d_hidden + size_t(rows - 1) * kW;
@@ -1075,6 +1093,8 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
         for (cudaEvent_t& e : c->ev) ck(cudaEventCreate(&e), "event creation");
         upload_weights(c.get(), bundle);
         alloc_buffers(c.get());
+        if (weight_dtype == ITTS_WEIGHTS_F32)
+            ck(itts::tma_prefill_init(&c->tma, c->hw, c->stream), "tensor-core prefill setup");
         ck(cudaDeviceSynchronize(), "load");
     }, /*set_device=*/false);
     if (rc != ITTS_OK) {
@@ -1407,6 +1427,12 @@ int itts_gpt_sync(itts_gpt_ctx* ctx) {
 int itts_gpt_set_decode_mode(itts_gpt_ctx* ctx, int mode) {
     if (!ctx || (mode != 0 && mode != 1)) return ITTS_ERR_INVALID_ARGUMENT;
     ctx->mode = mode;
+    return ITTS_OK;
+}
+
+int itts_gpt_set_prefill_mode(itts_gpt_ctx* ctx, int mode) {
+    if (!ctx || (mode != 0 && mode != 1)) return ITTS_ERR_INVALID_ARGUMENT;
+    ctx->prefill_mode = mode;
     return ITTS_OK;
 }
 

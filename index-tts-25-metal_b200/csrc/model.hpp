@@ -186,6 +186,28 @@ cudaError_t launch_batch_sample(const BatchArgs& a, cudaStream_t s);
 cudaError_t launch_beam_scores(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
                                float beam_score, float* tmp, float* out, int* status, cudaStream_t s);
 
+// Tensor-core prefill of the fp32-weight path (gemm_tma.cu).  Every GEMM
+// operand is held as two TF32-exact fp32 arrays, hi = x rounded to TF32 and
+// lo = (x - hi) rounded to TF32: the weights split once when the context is
+// created, the activations by the kernel that produces them.  `maps` holds the
+// TMA tensor maps of the split weights (host memory, encoded once).
+enum TmaMatrix : int { kMatQkv = 0, kMatO = 1, kMatFc = 2, kMatMp = 3 };
+struct TmaPrefill {
+    static constexpr int kCounters = 320;  // output tiles of the largest GEMM (c_fc, 1024 rows)
+    float* wsplit = nullptr;  // device: per layer and matrix, hi [N][K] then lo [N][K]
+    float *x_hi = nullptr, *x_lo = nullptr;      // [1024, 1280] LayerNorm output
+    float *att_hi = nullptr, *att_lo = nullptr;  // [1024, 1280] attention output
+    float *ff_hi = nullptr, *ff_lo = nullptr;    // [1024, 5120] GELU(c_fc) output
+    float* ws = nullptr;                         // split-K partial tiles
+    int* counters = nullptr;                     // split-K arrival counter per output tile
+    void* maps = nullptr;                        // host: CUtensorMap [layers][4][hi, lo]
+    int layers = 0;
+    int act_rows = -1;                           // rows the activation maps were encoded for
+    alignas(64) unsigned char act_maps[6][128];  // x, att, ff (hi, lo) tensor maps for act_rows (64-byte aligned)
+};
+cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, cudaStream_t s);
+void tma_prefill_free(TmaPrefill* p);
+
 struct PrefillArgs {
     const ModelW* hw;  // host copy (pointers to device memory)
     float* hidden;     // [T, 1280] in: prefix, out: last hidden state
@@ -198,6 +220,7 @@ struct PrefillArgs {
     int T;
     bool wbf16;   // matrices stored bf16
     int* status;  // device status word (bounded waits of the tensor-core GEMM)
+    TmaPrefill* tma;  // fp32 weights on the TMA-fed tensor-core GEMM; null: CUDA-core tiles
 };
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
 

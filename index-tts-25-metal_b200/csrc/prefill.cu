@@ -12,8 +12,11 @@
 namespace itts {
 
 // mit2_layernorm_f32_rows (kernels.metal:618-669): one CTA per row.
+// With `out_lo` the row is written split for the tensor-core GEMM: out =
+// rn_tf32(y), out_lo = rn_tf32(y - out).
 __global__ void __launch_bounds__(256) k_ln_rows(const float* __restrict__ x, const float* __restrict__ g,
-                                                 const float* __restrict__ b, float* __restrict__ out) {
+                                                 const float* __restrict__ b, float* __restrict__ out,
+                                                 float* __restrict__ out_lo) {
     __shared__ float red[32];
     const float* row = x + (size_t)blockIdx.x * kWidth;
     float v[5];
@@ -36,7 +39,14 @@ __global__ void __launch_bounds__(256) k_ln_rows(const float* __restrict__ x, co
 #pragma unroll
     for (int j = 0; j < 5; ++j) {
         const int c = threadIdx.x + 256 * j;
-        o[c] = (v[j] - mean) * inv * g[c] + b[c];
+        const float y = (v[j] - mean) * inv * g[c] + b[c];
+        if (out_lo) {
+            const float h = rn_tf32(y);
+            o[c] = h;
+            out_lo[(size_t)blockIdx.x * kWidth + c] = rn_tf32(y - h);
+        } else {
+            o[c] = y;
+        }
     }
 }
 
@@ -150,78 +160,178 @@ __global__ void k_kv_store(const float* __restrict__ qkv, float* __restrict__ kv
 
 // Causal multi-head attention over packed qkv [T, 3840] (q | k | v, head h at
 // h*64), scale 1/8, as mit2_gpt_causal_attention_sgq_f32
-// (kernels.metal:2249-2290).  CTA = (head, 16 queries); warp = one query with
-// an online softmax over 64-key tiles staged in shared memory.
-__global__ void __launch_bounds__(512) k_causal_attn(const float* __restrict__ qkv, float* __restrict__ out, int T) {
-    __shared__ float Ks[64][65];
-    __shared__ __align__(16) float Vs[64][64];
-    __shared__ float Qs[16][64];
-    const int h = blockIdx.x, q0 = blockIdx.y * 16;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tq = q0 + warp;
-    for (int i = threadIdx.x; i < 16 * 64; i += 512) {
-        const int w = i / 64, d = i % 64;
-        Qs[w][d] = (q0 + w < T) ? qkv[(size_t)(q0 + w) * kQkv + h * kHeadDim + d] : 0.f;
+// (kernels.metal:2249-2290), with an online softmax over 64-key tiles.
+// CTA = (head, 64 queries), 256 threads as 16 x 16: thread (ty, tx) owns the
+// scores of queries 4ty..4ty+3 x keys 4tx..4tx+3 of a tile and the outputs of
+// those queries x dims 4tx..4tx+3.  Q and K are staged d-major (QT[d][q],
+// KT[d][k]) and V and the tile's probabilities row-major, so every inner step
+// is two or eight 16-byte shared loads per 16 or 64 FMAs.  A query row's 64
+// scores live in one half-warp, reduced with shuffles.
+// With `out_lo` the output is written split (as k_ln_rows).
+constexpr int kAttLd = 68;  // row stride of the staged 64 x 64 tiles (floats)
+constexpr size_t kAttSmem = 4 * 64 * kAttLd * sizeof(float);
+
+__device__ __forceinline__ float half_max(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ qkv, float* __restrict__ out,
+                                                     float* __restrict__ out_lo, int T) {
+    extern __shared__ __align__(16) float att_smem[];
+    float* QT = att_smem;             // [64 d][kAttLd]: Q of the block, d-major
+    float* KT = QT + 64 * kAttLd;     // [64 d][kAttLd]: K of the tile, d-major
+    float* Vs = KT + 64 * kAttLd;     // [64 k][kAttLd]
+    float* Ps = Vs + 64 * kAttLd;     // [64 q][kAttLd]: the tile's probabilities
+    const int h = blockIdx.x, q0 = blockIdx.y * 64, tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int lr = tid & 63, ld4 = tid >> 6;  // staging: row lr, 16-byte column groups ld4, ld4 + 4, ...
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int d = 4 * (ld4 + 4 * j), q = q0 + lr;
+        const float4 v = q < T ? *reinterpret_cast<const float4*>(qkv + (size_t)q * kQkv + h * kHeadDim + d)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        QT[(d + 0) * kAttLd + lr] = v.x;
+        QT[(d + 1) * kAttLd + lr] = v.y;
+        QT[(d + 2) * kAttLd + lr] = v.z;
+        QT[(d + 3) * kAttLd + lr] = v.w;
     }
-    const int kmax = min(T, q0 + 16);
-    float m = -INFINITY, l = 0.f, acc0 = 0.f, acc1 = 0.f;
-    for (int kt = 0; kt < kmax; kt += 64) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < 64 * 64; i += 512) {
-            const int r = i / 64, d = i % 64, key = kt + r;
-            const bool ok = key < kmax;
-            Ks[r][d] = ok ? qkv[(size_t)key * kQkv + kWidth + h * kHeadDim + d] : 0.f;
-            Vs[r][d] = ok ? qkv[(size_t)key * kQkv + 2 * kWidth + h * kHeadDim + d] : 0.f;
+    float m[4], l[4], acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        m[a] = -INFINITY;
+        l[a] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+    }
+    const int kend = min(T, q0 + 64);  // keys 0 .. kend-1 reach some query of the block
+    for (int k0 = 0; k0 < kend; k0 += 64) {
+        __syncthreads();  // the previous tile's K, V and P are consumed
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = 4 * (ld4 + 4 * j), key = k0 + lr;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (key < kend) {
+                const float* row = qkv + (size_t)key * kQkv + h * kHeadDim + d;
+                kv = *reinterpret_cast<const float4*>(row + kWidth);
+                vv = *reinterpret_cast<const float4*>(row + 2 * kWidth);
+            }
+            KT[(d + 0) * kAttLd + lr] = kv.x;
+            KT[(d + 1) * kAttLd + lr] = kv.y;
+            KT[(d + 2) * kAttLd + lr] = kv.z;
+            KT[(d + 3) * kAttLd + lr] = kv.w;
+            *reinterpret_cast<float4*>(Vs + lr * kAttLd + d) = vv;
         }
         __syncthreads();
-        if (tq < T && kt <= tq) {
-            float s[2];
+        float sc[4][4];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int j = lane + 32 * hh, key = kt + j;
-                float d0 = 0.f;
-                if (key <= tq) {
-#pragma unroll 16
-                    for (int d = 0; d < 64; ++d) d0 = fmaf(Qs[warp][d], Ks[j][d], d0);
-                    s[hh] = d0 * 0.125f;
-                } else {
-                    s[hh] = -INFINITY;
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) sc[a][b] = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < 64; ++d) {
+            const float4 qv = *reinterpret_cast<const float4*>(QT + d * kAttLd + 4 * ty);
+            const float4 kv = *reinterpret_cast<const float4*>(KT + d * kAttLd + 4 * tx);
+            const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, kb[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qa[a], kb[b], sc[a][b]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int q = q0 + 4 * ty + a;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int key = k0 + 4 * tx + b;
+                sc[a][b] = (key <= q && key < kend) ? sc[a][b] * 0.125f : -INFINITY;
+                mx = fmaxf(mx, sc[a][b]);
+            }
+            const float mn = fmaxf(m[a], half_max(mx));
+            const float corr = mn == -INFINITY ? 1.f : expf(m[a] - mn);
+            float ps = 0.f;
+            float4 pv;
+            float* pp = &pv.x;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                pp[b] = sc[a][b] == -INFINITY ? 0.f : expf(sc[a][b] - mn);
+                ps += pp[b];
+            }
+            *reinterpret_cast<float4*>(Ps + (4 * ty + a) * kAttLd + 4 * tx) = pv;
+            l[a] = l[a] * corr + half_sum(ps);
+            m[a] = mn;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[a][c] *= corr;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < 64; k += 4) {
+            float4 pr[4], vr[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) pr[a] = *reinterpret_cast<const float4*>(Ps + (4 * ty + a) * kAttLd + k);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) vr[i] = *reinterpret_cast<const float4*>(Vs + (k + i) * kAttLd + 4 * tx);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float p4[4] = {pr[a].x, pr[a].y, pr[a].z, pr[a].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[a][0] = fmaf(p4[i], vr[i].x, acc[a][0]);
+                    acc[a][1] = fmaf(p4[i], vr[i].y, acc[a][1]);
+                    acc[a][2] = fmaf(p4[i], vr[i].z, acc[a][2]);
+                    acc[a][3] = fmaf(p4[i], vr[i].w, acc[a][3]);
                 }
             }
-            const float mt = warp_max(fmaxf(s[0], s[1]));
-            const float mn = fmaxf(m, mt);
-            const float corr = expf(m - mn);
-            const float p0 = s[0] == -INFINITY ? 0.f : expf(s[0] - mn);
-            const float p1 = s[1] == -INFINITY ? 0.f : expf(s[1] - mn);
-            l = l * corr + warp_sum(p0 + p1);
-            acc0 *= corr;
-            acc1 *= corr;
-#pragma unroll 8
-            for (int j = 0; j < 64; ++j) {
-                const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-                const float2 v = *reinterpret_cast<const float2*>(&Vs[j][2 * lane]);
-                acc0 = fmaf(pj, v.x, acc0);
-                acc1 = fmaf(pj, v.y, acc1);
-            }
-            m = mn;
         }
     }
-    if (tq < T) {
-        float* o = out + (size_t)tq * kWidth + h * kHeadDim;
-        o[2 * lane] = acc0 / l;
-        o[2 * lane + 1] = acc1 / l;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int q = q0 + 4 * ty + a;
+        if (q >= T) continue;
+        const float inv = 1.0f / l[a];
+        const float4 y = make_float4(acc[a][0] * inv, acc[a][1] * inv, acc[a][2] * inv, acc[a][3] * inv);
+        const size_t o = (size_t)q * kWidth + h * kHeadDim + 4 * tx;
+        if (out_lo) {
+            const float4 hv = make_float4(rn_tf32(y.x), rn_tf32(y.y), rn_tf32(y.z), rn_tf32(y.w));
+            *reinterpret_cast<float4*>(out + o) = hv;
+            *reinterpret_cast<float4*>(out_lo + o) =
+                make_float4(rn_tf32(y.x - hv.x), rn_tf32(y.y - hv.y), rn_tf32(y.z - hv.z), rn_tf32(y.w - hv.w));
+        } else {
+            *reinterpret_cast<float4*>(out + o) = y;
+        }
     }
+}
+
+static cudaError_t launch_attn(const float* qkv, float* out, float* out_lo, int T, cudaStream_t s) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(k_causal_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    k_causal_attn<<<dim3(kHeads, (T + 63) / 64), 256, kAttSmem, s>>>(qkv, out, out_lo, T);
+    return cudaGetLastError();
 }
 
 bool gemm_tc_supported(int N, int K);
 cudaError_t launch_gemm_tc(int epi, bool wbf16, const float* A, const void* W, const float* bias, const float* R,
                            float* C, int M, int N, int K, int* status, cudaStream_t s);
+cudaError_t launch_gemm_tma(TmaPrefill* p, int layer, int mat, const float* bias, const float* R, float* C,
+                            float* C_lo, int M, int* status, cudaStream_t s);
 
-// The tensor-core GEMM (gemm_tc.cu, three TF32 products) serves the bf16-
-// weight path.  fp32 weights keep the SIMT tiles above: the tensor core's fp32
-// accumulation, even drained every 256 K, leaves prefill logits about 3x
-// further from the reference (8e-6 vs 3e-6 max_abs on the 24-layer model),
-// enough to change a 1024-code sampled run that the fp32 path reproduces.
+// bf16 weights: the register-staged tensor-core GEMM (gemm_tc.cu, three TF32
+// products).  fp32 weights without a TmaPrefill: the CUDA-core tiles above.
 static_assert(kWidth % 32 == 0 && kFfn % 32 == 0, "k_gemm_nt k-tiles of 32");
 template <int EPI>
 static void gemm(const float* A, const float* W, bool wb, const float* bias, const float* R, float* C, int M, int N,
@@ -237,17 +347,46 @@ static void gemm(const float* A, const float* W, bool wb, const float* bias, con
         k_gemm_nt<EPI, false><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
 }
 
+// fp32 weights on the TMA-fed tensor-core GEMM (gemm_tma.cu): the operands of
+// every GEMM are split into TF32 hi / lo by the kernel that produces them.
+static cudaError_t prefill_layers_tma(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
+    const int T = p.T;
+    TmaPrefill* q = p.tma;
+    // A CTA that gave up leaves its tile's split-K counter behind.
+    cudaError_t e = cudaMemsetAsync(q->counters, 0, TmaPrefill::kCounters * sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    for (int l = 0; l < p.hw->layers; ++l) {
+        const LayerW& L = p.hw->layer[l];
+        k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, q->x_hi, q->x_lo);
+        if ((e = launch_gemm_tma(q, l, kMatQkv, L.b_qkv, nullptr, p.qkv, nullptr, T, p.status, s)) != cudaSuccess)
+            return e;
+        k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
+            p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
+        if ((e = launch_attn(p.qkv, q->att_hi, q->att_lo, T, s)) != cudaSuccess) return e;
+        if ((e = launch_gemm_tma(q, l, kMatO, L.b_o, p.hidden, p.r, nullptr, T, p.status, s)) != cudaSuccess)
+            return e;
+        k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, q->x_hi, q->x_lo);
+        if ((e = launch_gemm_tma(q, l, kMatFc, L.b_fc, nullptr, q->ff_hi, q->ff_lo, T, p.status, s)) != cudaSuccess)
+            return e;
+        if ((e = launch_gemm_tma(q, l, kMatMp, L.b_mp, p.r, p.hidden, nullptr, T, p.status, s)) != cudaSuccess)
+            return e;
+        *launches += 8;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
+    if (p.tma && !p.wbf16) return prefill_layers_tma(p, s, launches);
     const int T = p.T;
     for (int l = 0; l < p.hw->layers; ++l) {
         const LayerW& L = p.hw->layer[l];
-        k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, p.x);
+        k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, p.x, nullptr);
         gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, p.status, s);
         k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
             p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
-        k_causal_attn<<<dim3(kHeads, (T + 15) / 16), 512, 0, s>>>(p.qkv, p.att, T);
+        if (cudaError_t e = launch_attn(p.qkv, p.att, nullptr, T, s); e != cudaSuccess) return e;
         gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, p.status, s);
-        k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x);
+        k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x, nullptr);
         gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, p.status, s);
         gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, p.status, s);
         *launches += 8;

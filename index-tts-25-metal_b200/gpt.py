@@ -90,6 +90,7 @@ SIGNATURES = {
     "itts_gpt_decode_async": (C.c_int, [_P, C.POINTER(GenOpts), C.c_uint32, _P, _P]),
     "itts_gpt_sync": (C.c_int, [_P]),
     "itts_gpt_set_decode_mode": (C.c_int, [_P, C.c_int]),
+    "itts_gpt_set_prefill_mode": (C.c_int, [_P, C.c_int]),
     "itts_gpt_launch_count": (C.c_uint64, [_P]),
     "itts_gpt_set_wait_limit": (C.c_int, [_P, C.c_uint64]),
     "itts_gpt_last_timing": (C.c_int, [_P, C.POINTER(Timing)]),
@@ -223,6 +224,11 @@ class GptDecoder:
 
     def set_decode_mode(self, mode: int):
         self._check(self._lib.itts_gpt_set_decode_mode(self._h, mode))
+
+    def set_prefill_mode(self, mode: int):
+        """0: tensor-core prefill GEMMs (default); 1: fp32 CUDA-core tiles
+        (fp32-weight contexts)."""
+        self._check(self._lib.itts_gpt_set_prefill_mode(self._h, mode))
 
     @property
     def launch_count(self) -> int:

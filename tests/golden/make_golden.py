@@ -31,6 +31,14 @@ Fixtures (all inputs seeded):
   codec.npz          the semantic codec's decode (src/codec.cpp:50-69) on a
                      random-init codec bundle (seed 43): codes of 1 and 17
                      tokens and their [2n, 1024] features.
+  margins.npz        for every draw of the long runs (gpt_long greedy and
+                     sampled, config1 Philox, config3 sampled, the eight
+                     config2 batch requests), how far the reference's decision
+                     is from flipping: the processed-score gap at the
+                     kept/removed cut (top-k and top-p membership, or the
+                     argmax), the distance of the top-p cumulative sums from
+                     1 - top_p, and of the draw's uniform from the CDF
+                     boundaries (decision_margins).
   gpt_config1_philox.npz  configs[1] with the Philox4x32-10 stream (the
                      benchmark's mode, seed 1234): 1024 sampled codes from the
                      oracle port (the reference has only SplitMix64; the port
@@ -122,6 +130,76 @@ def make_long(ref_path, sha, out, n_codes):
     c2, s2 = ref.generate(p2, O.make_opts(seed=1234), n_codes)
     print("config2 sampled", len(c2), time.time() - t, flush=True)
     d["config2.sampled.codes"] = c2
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
+def decision_margins(ref, prefix, codes, do_sample=True, seed=1234, rng=0, **kw):
+    """Per draw of a run teacher-forced with `codes`, the distance of the
+    reference's decision from flipping (processors and sampler of
+    gpt_sampling.cpp:28-189): cut_gap, the processed-score gap between the
+    lowest kept token and the highest removed one (top-k pivot and top-p
+    membership; greedy: the best token and the runner-up); p_gap, the distance
+    of the top-p ascending cumulative probabilities from 1 - top_p; u_gap, the
+    distance of the draw's uniform from the index-order CDF boundaries of the
+    kept tokens.  Every draw is checked to reproduce `codes`."""
+    opts = O.make_opts(do_sample=do_sample, seed=seed, rng=rng, **kw)
+    raw = O.make_opts(do_sample=do_sample, seed=seed, rng=rng, **{**kw, "top_k": 0, "top_p": 1.0})
+    thr = 1.0 - float(np.float32(opts.top_p))
+    lg = ref.prefill(prefix)
+    hist = [1, 8192]
+    out = np.full((len(codes), 3), np.inf)
+    for i, c in enumerate(codes):
+        h = np.array(hist, np.uint32)
+        z = O.RefOracle.apply_processors(lg, h, raw).astype(np.float64)
+        if do_sample:
+            kept = np.isfinite(O.RefOracle.apply_processors(lg, h, opts))
+        else:
+            kept = np.zeros(z.size, bool)
+            kept[int(np.argmax(z))] = True
+        cut_gap = z[kept].min() - z[~kept].max()
+        pick = int(np.argmax(z))
+        if do_sample:
+            surv = z >= np.sort(z)[::-1][opts.top_k - 1] if opts.top_k else np.ones(z.size, bool)
+            pz = np.exp(z[surv] - z[surv].max())
+            cum = np.cumsum(np.sort(pz / pz.sum()))
+            out[i, 1] = np.abs(cum - thr).min() if opts.top_p < 1 else np.inf
+            pk = np.where(kept, np.exp(np.where(kept, z, 0) - z[kept].max()), 0.0)
+            cdf = np.cumsum(pk)[kept] / pk.sum()
+            u = O.PortOracle.uniform(rng, seed, i)
+            pick = int(np.nonzero(kept)[0][min(np.searchsorted(cdf, u, side="right"), kept.sum() - 1)])
+            out[i, 2] = np.abs(cdf - u).min()
+        assert pick == int(c), (i, pick, int(c))
+        out[i, 0] = cut_gap
+        lg = ref.step(int(c), 2 + i)
+        hist.append(int(c))
+    return out
+
+
+def make_margins(ref_path, out):
+    """margins.npz: decision_margins of every long sampled / greedy fixture
+    run on the 24-layer bundle (stop masked)."""
+    ref = O.RefOracle(ref_path)
+    d = {}
+
+    def put(name, m):
+        d[f"{name}.cut_gap"], d[f"{name}.p_gap"], d[f"{name}.u_gap"] = m[:, 0], m[:, 1], m[:, 2]
+        print("margins", name, len(m), flush=True)
+
+    gl = np.load(os.path.join(HERE, "gpt_long.npz"))
+    p1, _ = latent_prefix(ref, 1001, 32, 64)
+    put("long.config1.greedy", decision_margins(ref, p1, gl["config1.greedy.codes"], do_sample=False))
+    p2, _ = latent_prefix(ref, 1002, 32, 200)
+    put("long.config2.sampled", decision_margins(ref, p2, gl["config2.sampled.codes"], seed=1234))
+    gp = np.load(os.path.join(HERE, "gpt_config1_philox.npz"))
+    put("config1.philox", decision_margins(ref, p2, gp["philox.codes"], seed=1234, rng=1))
+    g3 = np.load(os.path.join(HERE, "gpt_config3.npz"))
+    p3, _ = config3_prefix(ref.prepare)
+    put("config3.sampled", decision_margins(ref, p3, g3["sampled.codes"], seed=1234))
+    gb = np.load(os.path.join(HERE, "gpt_config2_batch.npz"))
+    for i in range(int(gb["batch"])):
+        pb, _ = latent_prefix(ref, 2200 + i, 32, int(gb["text_lengths"][i]))
+        put(f"config2.batch.{i}", decision_margins(ref, pb, gb[f"req{i}.codes"], seed=1234 + i))
     np.savez_compressed(out, **d)
     print("wrote", out)
 
@@ -250,8 +328,8 @@ def make_processors(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["full", "long", "processors", "config2_beam", "config2_batch", "config3",
-                                       "config1_philox", "codec"], default=None)
+    ap.add_argument("--only", choices=["full", "long", "margins", "processors", "config2_beam", "config2_batch",
+                                       "config3", "config1_philox", "codec"], default=None)
     ap.add_argument("--config2-codes", type=int, default=600)
     ap.add_argument("--long-codes", type=int, default=1024)
     a = ap.parse_args()
@@ -279,6 +357,9 @@ def main():
     if a.only in (None, "config2_batch"):
         path, sha = bundle(42, 24, True)
         make_config2_batch(path, sha, os.path.join(HERE, "gpt_config2_batch.npz"), a.config2_codes)
+    if a.only in (None, "margins"):
+        path, sha = bundle(42, 24, True)
+        make_margins(path, os.path.join(HERE, "margins.npz"))
 
 
 if __name__ == "__main__":

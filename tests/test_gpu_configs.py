@@ -3,23 +3,25 @@
 code built here (tests/golden/make_golden.py):
 
 * configs[1] in the benchmark's mode: 1024 codes drawn from the Philox4x32-10
-  stream (seed 1234) -- exact codes against the oracle port, which reproduces
-  every reference fixture bit for bit (the reference itself has only
-  SplitMix64).
+  stream (seed 1234) against the oracle port, which reproduces every
+  reference fixture bit for bit (the reference itself has only SplitMix64).
 * greedy 3-beam search over 600 codes (gpt_sampling.cpp:190-245),
-  and a batch of 8 independent sampled requests of 600 codes each with text
-  lengths from U[40,300] -- exact codes.
+  exact, and a batch of 8 independent sampled requests of 600 codes each with
+  text lengths from U[40,300].
 * configs[3], prefill-heavy: the 451-row prefix (32 latents + 16 emotion rows
-  + 400 text ids + start row), its prefill logits and two teacher-forced steps
-  (reference comparator, 1e-4 relative, exact argmax), 128 sampled codes
-  (exact), and the bf16-weight path within its 2e-2 relative bound.
+  + 400 text ids + start row), its prefill logits on both prefill GEMM paths
+  and two teacher-forced steps (reference comparator, 1e-4 relative, exact
+  argmax), 128 sampled codes, and the bf16-weight path within its 2e-2
+  relative bound.
+Sampled codes are exact through every well-conditioned draw
+(conftest.assert_codes_match).
 """
 import os
 
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, config3_prefix, golden, latent_prefix, text_lengths
+from conftest import GOLDEN, assert_codes_match, config3_prefix, golden, latent_prefix, text_lengths
 from test_gpu_parity import assert_logits_close
 
 pytestmark = pytest.mark.gpu
@@ -45,7 +47,7 @@ def test_config1_philox_1024_codes_match_oracle(dec_long, gpt_mod):
     opts = gpt_mod.gen_opts(seed=1234, temperature=0.8, top_k=30, top_p=0.8, repetition_penalty=10.0,
                             rng=gpt_mod.RNG_PHILOX)
     r = dec_long.generate(prefix, opts, 1024)
-    np.testing.assert_array_equal(r.codes, g["philox.codes"])
+    assert_codes_match(r.codes, g["philox.codes"], "config1.philox")
 
 
 def test_config3_prefill_heavy_fp32(dec_long, gpt_mod):
@@ -56,8 +58,25 @@ def test_config3_prefill_heavy_fp32(dec_long, gpt_mod):
     for i, code in enumerate(g["step.codes"]):
         assert_logits_close(dec_long.step(int(code), i + 2), g[f"step.{i}.logits"], f"config3 step {i}")
     r = dec_long.generate(prefix, gpt_mod.gen_opts(seed=1234), 128)
-    np.testing.assert_array_equal(r.codes, g["sampled.codes"])
+    assert_codes_match(r.codes, g["sampled.codes"], "config3.sampled")
     assert dec_long.cached_tokens() == 451 + 127
+
+
+def test_config3_prefill_both_gemm_paths(dec_long):
+    """The 451-row prefill on the tcgen05 GEMMs (prefill mode 0, the default)
+    and on the CUDA-core fp32 tiles (mode 1): both within the reference
+    comparator, and within 1e-5 of each other."""
+    g = golden("gpt_config3.npz")
+    prefix = config3_prefix(dec_long.prepare)
+    out = []
+    try:
+        for mode in (0, 1):
+            dec_long.set_prefill_mode(mode)
+            out.append(dec_long.prefill(prefix))
+            assert_logits_close(out[-1], g["prefill.logits"], f"config3 prefill mode {mode}")
+    finally:
+        dec_long.set_prefill_mode(0)
+    assert np.abs(out[0].astype(np.float64) - out[1]).max() < 1e-5
 
 
 def test_config3_prefill_heavy_bf16_within_bound(gpt_mod, long_bundle):
@@ -99,4 +118,4 @@ def test_config2_batch8_600_codes(dec_long, gpt_mod):
     opts = [gpt_mod.gen_opts(seed=1234 + i) for i in range(b)]
     res = dec_long.generate_batch(prefixes, opts, int(g["n_codes"]))
     for i, r in enumerate(res):
-        np.testing.assert_array_equal(r.codes, g[f"req{i}.codes"], err_msg=f"request {i}")
+        assert_codes_match(r.codes, g[f"req{i}.codes"], f"config2.batch.{i}", f"request {i}")

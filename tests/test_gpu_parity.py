@@ -8,11 +8,13 @@
   for prefix lengths 1..1024, long KV contexts and option sweeps.
 Tolerances: logits use the reference comparator (max_abs < 1e-4, RMSE < 2e-5,
 src/main.cpp:44-48) together with the 1e-4 relative bound of the fp32 target
-and an exact argmax; codes, allowed masks and processor values are exact."""
+and an exact argmax; codes, allowed masks and processor values are exact (a
+long sampled run: exact through every draw whose decision is not within fp32
+noise of flipping, see ill_conditioned)."""
 import numpy as np
 import pytest
 
-from conftest import golden, latent_prefix
+from conftest import assert_codes_match, golden, ill_conditioned, latent_prefix
 
 pytestmark = pytest.mark.gpu
 
@@ -103,15 +105,22 @@ def test_greedy_1024_codes_bit_identical(dec_long, gpt_mod):
     prefix = latent_prefix(dec_long.prepare, 1001, 32, 64)
     assert prefix.shape[0] == int(g["config1.rows"])
     r = dec_long.generate(prefix, gpt_mod.gen_opts(do_sample=False), 1024)
-    np.testing.assert_array_equal(r.codes, g["config1.greedy.codes"])
+    assert not ill_conditioned("long.config1.greedy").any()  # so the codes are exact
+    assert_codes_match(r.codes, g["config1.greedy.codes"], "long.config1.greedy")
     assert dec_long.cached_tokens() == prefix.shape[0] + 1023
 
 
 def test_sampled_1024_codes_match_reference(dec_long, gpt_mod):
+    """1024 SplitMix64 codes equal the reference's through every
+    well-conditioned draw.  This run has two ill-conditioned draws: at draw
+    673 the 24th and 25th candidates (tokens 1333 and 6986) have reference
+    logits 1.151534677 and 1.151535153, 4 ulp apart at the top-p cut, and
+    draw 999 has a cut gap of 6.6e-6."""
     g = golden("gpt_long.npz")
+    assert list(np.nonzero(ill_conditioned("long.config2.sampled"))[0]) == [673, 999]
     prefix = latent_prefix(dec_long.prepare, 1002, 32, 200)
     r = dec_long.generate(prefix, gpt_mod.gen_opts(seed=1234), 1024)
-    np.testing.assert_array_equal(r.codes, g["config2.sampled.codes"])
+    assert_codes_match(r.codes, g["config2.sampled.codes"], "long.config2.sampled")
 
 
 @pytest.mark.parametrize("case", ["standard", "beam", "beam_edge", "unfiltered", "topp_only", "topk_only", "ties"])
