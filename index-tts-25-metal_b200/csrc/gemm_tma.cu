@@ -171,7 +171,7 @@ struct GemmArgs {
     int* status;
 };
 
-enum GemmEpi : int { kEpiBias = 0, kEpiGelu = 1, kEpiResid = 2 };
+enum GemmEpi : int { kEpiBias = TmaEpiBias, kEpiGelu = TmaEpiGelu, kEpiResid = TmaEpiResid, kEpiSwiGLU = TmaEpiSwiGLU };
 
 // CTA i owns units [i U / G, (i + 1) U / G) of the tile-major (tile, K block)
 // sequence: every CTA gets the same number of K blocks (to one), whatever the
@@ -196,6 +196,18 @@ __device__ __forceinline__ float* slot(const GemmArgs& g, int i, int t) {
 template <int EPI>
 __device__ __forceinline__ void store_out(const GemmArgs& g, int m, int n, float4 v, float4 b) {
     float4 y = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+    if (EPI == kEpiSwiGLU) {
+        // W rows interleave gate and up (row 2r = gate_r, 2r + 1 = up_r): the
+        // four columns are (gate, up) of outputs n/2 and n/2 + 1 of C[M][N/2],
+        // silu(gate) * up as mit2_silu_mul_f32 (kernels.metal:363-374), split
+        // into hi / lo for the next GEMM.
+        const float s0 = y.x / (1.0f + expf(-y.x)) * y.y, s1 = y.z / (1.0f + expf(-y.z)) * y.w;
+        const size_t o = size_t(m) * (g.N / 2) + n / 2;
+        const float h0 = rn_tf32(s0), h1 = rn_tf32(s1);
+        *reinterpret_cast<float2*>(g.C + o) = make_float2(h0, h1);
+        *reinterpret_cast<float2*>(g.C_lo + o) = make_float2(rn_tf32(s0 - h0), rn_tf32(s1 - h1));
+        return;
+    }
     const size_t o = size_t(m) * g.N + n;
     if (EPI == kEpiGelu) {
         y = make_float4(gelu_ref(y.x), gelu_ref(y.y), gelu_ref(y.z), gelu_ref(y.w));
@@ -211,6 +223,11 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int m, int n, float
         y = make_float4(r.x + y.x, r.y + y.y, r.z + y.z, r.w + y.w);
     }
     *reinterpret_cast<float4*>(g.C + o) = y;
+}
+
+// Bias at columns n..n+3, or zeros without a bias.
+__device__ __forceinline__ float4 bias4(const GemmArgs& g, int n) {
+    return g.bias ? __ldg(reinterpret_cast<const float4*>(g.bias + n)) : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 __device__ __forceinline__ void drain_sync() { asm volatile("bar.sync 2, %0;" ::"n"(32 * kDrainWarps) : "memory"); }
@@ -370,8 +387,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int col = (lane & 15) * 4;
             float4 bias2[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
             if (!part) {
-                bias2[0] = __ldg(reinterpret_cast<const float4*>(g.bias + n0 + col));
-                bias2[1] = __ldg(reinterpret_cast<const float4*>(g.bias + n0 + kDrainCols + col));
+                bias2[0] = bias4(g, n0 + col);
+                bias2[1] = bias4(g, n0 + kDrainCols + col);
             }
             for (int pass = 0; pass < 4; ++pass) {
                 const int rh = pass >> 1, ch = pass & 1;
@@ -408,7 +425,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 drain_sync();
                 if (sm.last) {
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(g.bias + n0 + 4 * lane));
+                    const float4 b = bias4(g, n0 + 4 * lane);
                     const float* p0 = slot(g, first, t) + 4 * lane;
                     if (nc <= 3) {  // the common case: four rows' loads in flight at once
                         const float* p1 = slot(g, first + 1, t) + 4 * lane;
@@ -609,6 +626,32 @@ cudaError_t tma_prefill_rows(TmaPrefill* p, int rows) {
     return cudaSuccess;
 }
 
+namespace {
+
+// One GEMM C = epi(A W^T + bias) from A's and W's (hi, lo) tensor maps.
+cudaError_t run_gemm(const CUtensorMap* ma, const CUtensorMap* mw, int epi, const float* bias, const float* R,
+                     float* C, float* C_lo, int M, int N, int K, float* ws, int* counters, int counters_n,
+                     int* status, cudaStream_t s) {
+    if (M < 1 || N % GN || K % GK || K < GK) return cudaErrorInvalidValue;
+    const int kbt = K / GK, tiles = ((M + GM - 1) / GM) * (N / GN);
+    if (tiles > counters_n) return cudaErrorInvalidValue;
+    // One CTA per SM, every CTA the same number of K blocks (to one); at least
+    // one accumulation chunk per CTA, and few tiles spread over at most
+    // kCtasPerTile CTAs each.
+    const long long units = (long long)tiles * kbt;
+    const int ctas = int(std::max(1LL, std::min({(long long)std::min(sm_count(), kMaxCtas),
+                                                 (long long)kCtasPerTile * tiles, units / kChunk})));
+    GemmArgs g{bias, R, C, C_lo, M, N, K, kbt, N / GN, ctas, units, ws, counters, status};
+    switch (epi) {
+        case kEpiGelu: return launch_epi<kEpiGelu>(ma, mw, g, s);
+        case kEpiResid: return launch_epi<kEpiResid>(ma, mw, g, s);
+        case kEpiSwiGLU: return C_lo ? launch_epi<kEpiSwiGLU>(ma, mw, g, s) : cudaErrorInvalidValue;
+        default: return launch_epi<kEpiBias>(ma, mw, g, s);
+    }
+}
+
+}  // namespace
+
 // One prefill GEMM of layer `layer`: matrix `mat` (TmaMatrix) against the
 // split activation that feeds it (x for qkv and c_fc, att for c_proj, ff for
 // mlp.c_proj).
@@ -619,17 +662,33 @@ cudaError_t launch_gemm_tma(TmaPrefill* p, int layer, int mat, const float* bias
     CUtensorMap ma[2];
     std::memcpy(ma, p->act_maps[mat == kMatO ? 2 : mat == kMatMp ? 4 : 0], sizeof ma);
     const CUtensorMap* mw = &wmaps(p)[(layer * 4 + mat) * 2];
-    const int N = kMatN[mat], K = kMatK[mat], kbt = K / GK, tiles = ((M + GM - 1) / GM) * (N / GN);
-    // One CTA per SM, every CTA the same number of K blocks (to one); at least
-    // one accumulation chunk per CTA, and few tiles spread over at most
-    // kCtasPerTile CTAs each.
-    const long long units = (long long)tiles * kbt;
-    const int ctas = int(std::max(1LL, std::min({(long long)std::min(sm_count(), kMaxCtas),
-                                                 (long long)kCtasPerTile * tiles, units / kChunk})));
-    GemmArgs g{bias, R, C, C_lo, M, N, K, kbt, N / GN, ctas, units, p->ws, p->counters, status};
-    if (mat == kMatFc) return launch_epi<kEpiGelu>(ma, mw, g, s);
-    if (mat == kMatQkv) return launch_epi<kEpiBias>(ma, mw, g, s);
-    return launch_epi<kEpiResid>(ma, mw, g, s);
+    const int epi = mat == kMatFc ? kEpiGelu : mat == kMatQkv ? kEpiBias : kEpiResid;
+    return run_gemm(ma, mw, epi, bias, R, C, C_lo, M, kMatN[mat], kMatK[mat], p->ws, p->counters,
+                    TmaPrefill::kCounters, status, s);
+}
+
+cudaError_t tma_make_map(TmaMap* m, const float* base, uint64_t rows, uint64_t cols) {
+    static_assert(sizeof(TmaMap) == sizeof(CUtensorMap), "tensor map storage");
+    CUtensorMap t;
+    const cudaError_t e = make_map(&t, base, rows, cols);
+    if (e == cudaSuccess) std::memcpy(m->bytes, &t, sizeof t);
+    return e;
+}
+
+cudaError_t tma_split(const float* src, float* hi, float* lo, size_t n, cudaStream_t s) {
+    if (n % 4) return cudaErrorInvalidValue;
+    k_split_tf32<<<592, 256, 0, s>>>(src, hi, lo, n / 4);
+    return cudaGetLastError();
+}
+
+size_t tma_workspace_floats() { return kWsFloats; }
+
+cudaError_t tma_gemm(const TmaGemm& q, cudaStream_t s) {
+    CUtensorMap ma[2], mw[2];
+    std::memcpy(ma, q.a, sizeof ma);
+    std::memcpy(mw, q.w, sizeof mw);
+    return run_gemm(ma, mw, q.epi, q.bias, q.R, q.C, q.C_lo, q.M, q.N, q.K, q.ws, q.counters, q.counters_n,
+                    q.status, s);
 }
 
 }  // namespace itts

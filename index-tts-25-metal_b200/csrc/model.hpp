@@ -206,6 +206,36 @@ struct TmaPrefill {
     alignas(64) unsigned char act_maps[6][128];  // x, att, ff (hi, lo) tensor maps for act_rows (64-byte aligned)
 };
 cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, cudaStream_t s);
+
+// The same GEMM for other models (gemm_tma.cu): C = epi(A W^T + bias), A
+// [M][K] and W [N][K] each given by the tensor maps of its TF32 hi and lo
+// arrays (tma_make_map; split with tma_split).  N % 128 == 0, K % 32 == 0.
+enum TmaEpi : int {
+    TmaEpiBias = 0,    // C = A W^T + bias (bias may be null)
+    TmaEpiGelu = 1,    // GELU (GPT-2 tanh form); with C_lo the output is split hi / lo
+    TmaEpiResid = 2,   // C = R + A W^T + bias
+    TmaEpiSwiGLU = 3,  // W rows interleave gate / up: C, C_lo [M][N/2] = split(silu(gate) * up)
+};
+struct TmaMap {
+    alignas(64) unsigned char bytes[128];
+};
+struct TmaGemm {
+    const TmaMap* a;  // [2]: A hi, A lo
+    const TmaMap* w;  // [2]: W hi, W lo
+    const float* bias;
+    const float* R;
+    float* C;
+    float* C_lo;
+    int M, N, K, epi;
+    float* ws;         // tma_workspace_floats() floats
+    int* counters;     // >= output tiles, zeroed
+    int counters_n;
+    int* status;
+};
+cudaError_t tma_make_map(TmaMap* m, const float* base, uint64_t rows, uint64_t cols);
+cudaError_t tma_split(const float* src, float* hi, float* lo, size_t n, cudaStream_t s);
+size_t tma_workspace_floats();
+cudaError_t tma_gemm(const TmaGemm& g, cudaStream_t s);
 void tma_prefill_free(TmaPrefill* p);
 
 struct PrefillArgs {

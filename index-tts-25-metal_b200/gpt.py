@@ -102,6 +102,15 @@ SIGNATURES = {
     "itts_codec_destroy": (None, [_P]),
     "itts_codec_last_error": (C.c_char_p, [_P]),
     "itts_codec_decode": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t]),
+    # include/itts_qwen.h
+    "itts_qwen_create": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_P)]),
+    "itts_qwen_destroy": (None, [_P]),
+    "itts_qwen_last_error": (C.c_char_p, [_P]),
+    "itts_qwen_prefill": (C.c_int, [_P, _P, C.c_size_t, _P]),
+    "itts_qwen_step": (C.c_int, [_P, C.c_uint32, _P]),
+    "itts_qwen_generate": (C.c_int, [_P, _P, C.c_size_t, C.c_uint32, _P, C.c_size_t, C.POINTER(C.c_uint32)]),
+    "itts_qwen_cached_tokens": (C.c_uint32, [_P]),
+    "itts_qwen_last_timing": (C.c_int, [_P, _P]),
 }
 
 _lib = None
@@ -404,3 +413,72 @@ class SemanticCodec:
         if rc != OK:
             _raise(rc, self._lib.itts_codec_last_error(self._h).decode())
         return out[:2 * c.size]
+
+
+QWEN_VOCAB = 151936
+QWEN_EOS = 151643
+
+
+class QwenTiming(C.Structure):
+    _fields_ = [("prefill_ms", C.c_float), ("decode_ms", C.c_float), ("steps", C.c_uint32), ("prompt", C.c_uint32)]
+
+
+class QwenDecoder:
+    """The reference's itts25::QwenDecoder (include/itts25/qwen.hpp:6-19) over
+    include/itts_qwen.h: prefill / step logits and greedy generate on the B200."""
+
+    def __init__(self, bundle_dir: str, device: int = 0):
+        self._lib = load_library()
+        h = C.c_void_p()
+        rc = self._lib.itts_qwen_create(bundle_dir.encode(), device, C.byref(h))
+        if rc != OK:
+            _raise(rc, self._lib.itts_qwen_last_error(None).decode())
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.itts_qwen_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, rc):
+        if rc != OK:
+            _raise(rc, self._lib.itts_qwen_last_error(self._h).decode())
+
+    def prefill(self, ids) -> np.ndarray:
+        i = _u32(ids)
+        out = np.empty(QWEN_VOCAB, np.float32)
+        self._check(self._lib.itts_qwen_prefill(self._h, _ptr(i), i.size, _ptr(out)))
+        return out
+
+    def step(self, token: int) -> np.ndarray:
+        out = np.empty(QWEN_VOCAB, np.float32)
+        self._check(self._lib.itts_qwen_step(self._h, int(token), _ptr(out)))
+        return out
+
+    def generate(self, ids, maximum: int = 1024) -> np.ndarray:
+        i = _u32(ids)
+        out = np.zeros(max(1, maximum), np.uint32)
+        n = C.c_uint32()
+        self._check(self._lib.itts_qwen_generate(self._h, _ptr(i), i.size, int(maximum), _ptr(out), out.size,
+                                                 C.byref(n)))
+        return out[:n.value].copy()
+
+    def cached_tokens(self) -> int:
+        return int(self._lib.itts_qwen_cached_tokens(self._h))
+
+    def last_timing(self) -> QwenTiming:
+        t = QwenTiming()
+        self._check(self._lib.itts_qwen_last_timing(self._h, C.byref(t)))
+        return t

@@ -177,6 +177,86 @@ def write_synthetic_codec_bundle(path: str, *, seed: int = 43, std: float = 0.02
     return digest
 
 
+QWEN_VOCAB = 151936
+QWEN_EOS = 151643
+
+
+def qwen_tensor_specs():
+    """Ordered (name, shape, kind) list of the Qwen3-0.6B decoder
+    (src/qwen.cpp:5-14 shape checks and the tensors run() reads): tied
+    embedding / head 151936 x 1024, 28 layers of q 2048 x 1024, k and v
+    1024 x 1024, o 1024 x 2048, per-head q/k RMSNorm weights [128], input and
+    post-attention RMSNorm weights [1024], SwiGLU gate / up 3072 x 1024 and
+    down 1024 x 3072, then the final RMSNorm weight."""
+    specs = [("qwen.model.embed_tokens.weight", (QWEN_VOCAB, 1024), "mat")]
+    for i in range(28):
+        p = f"qwen.model.layers.{i}"
+        specs += [(f"{p}.input_layernorm.weight", (1024,), "ln_w"),
+                  (f"{p}.self_attn.q_proj.weight", (2048, 1024), "mat"),
+                  (f"{p}.self_attn.k_proj.weight", (1024, 1024), "mat"),
+                  (f"{p}.self_attn.v_proj.weight", (1024, 1024), "mat"),
+                  (f"{p}.self_attn.q_norm.weight", (128,), "ln_w"),
+                  (f"{p}.self_attn.k_norm.weight", (128,), "ln_w"),
+                  (f"{p}.self_attn.o_proj.weight", (1024, 2048), "mat"),
+                  (f"{p}.post_attention_layernorm.weight", (1024,), "ln_w"),
+                  (f"{p}.mlp.gate_proj.weight", (3072, 1024), "mat"),
+                  (f"{p}.mlp.up_proj.weight", (3072, 1024), "mat"),
+                  (f"{p}.mlp.down_proj.weight", (1024, 3072), "mat")]
+    specs.append(("qwen.model.norm.weight", (1024,), "ln_w"))
+    return specs
+
+
+def write_synthetic_qwen_bundle(path: str, *, seed: int = 44, std: float = 0.02, eos_gain: float = 1.0,
+                                alignment: int = 256, reuse: bool = True) -> str:
+    """Random-init Qwen3-0.6B bundle (target index-tts2.5, 596 M fp32
+    parameters, 2.4 GB) at ``path``; returns the SHA-256 of ``weights.bin``
+    (an existing complete bundle with the same arguments is reused).  Matrices
+    and the embedding N(0, std), RMSNorm weights 1 + N(0, std); the EOS row of
+    the tied embedding is multiplied by ``eos_gain`` so that greedy decoding
+    of a random model reaches EOS (QwenDecoder::generate requires it)."""
+    args = dict(kind="qwen", seed=seed, std=std, eos_gain=eos_gain, alignment=alignment)
+    os.makedirs(path, exist_ok=True)
+    marker = os.path.join(path, ".complete")
+    if reuse and bundle_complete(path):
+        with open(marker) as f:
+            rec = json.load(f)
+        if rec.get("args") == args:
+            return rec["sha256"]
+    if os.path.exists(marker):
+        os.remove(marker)
+    records, offset, h = [], alignment, hashlib.sha256()
+    with open(os.path.join(path, "weights.bin"), "wb") as f:
+        header = b"MIT2" + struct.pack("<II", 1, alignment)
+        header += b"\0" * (alignment - len(header))
+        f.write(header)
+        h.update(header)
+        for idx, (name, shape, kind) in enumerate(qwen_tensor_specs()):
+            v = _tensor_values(seed, idx, shape, kind, std)
+            if name == "qwen.model.embed_tokens.weight" and eos_gain != 1.0:
+                v[QWEN_EOS * 1024:(QWEN_EOS + 1) * 1024] *= np.float32(eos_gain)
+            raw = v.tobytes()
+            f.write(raw)
+            h.update(raw)
+            records.append({"name": name, "shape": list(shape), "dtype": "f32", "offset": offset,
+                            "nbytes": len(raw), "component": "qwen"})
+            offset += len(raw)
+            pad = (-offset) % alignment
+            if pad:
+                f.write(b"\0" * pad)
+                h.update(b"\0" * pad)
+                offset += pad
+    manifest = {"format": "MIT2", "version": 1, "alignment": alignment, "endianness": "little",
+                "target": "index-tts2.5", "weights_file": "weights.bin",
+                "synthetic": {"seed": seed, "std": std, "init": "normal", "component": "qwen",
+                              "eos_gain": eos_gain}, "tensors": records}
+    with open(os.path.join(path, "manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=0)
+    digest = h.hexdigest()
+    with open(marker, "w") as f:
+        json.dump({"args": args, "sha256": digest}, f)
+    return digest
+
+
 def bundle_complete(path: str) -> bool:
     return os.path.exists(os.path.join(path, "manifest.json")) and \
         os.path.exists(os.path.join(path, ".complete"))

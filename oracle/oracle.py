@@ -264,6 +264,61 @@ class RefCodec:
             self.h = None
 
 
+QWEN_VOCAB = 151936
+
+
+class RefQwen:
+    """The reference's own QwenDecoder (src/qwen.cpp) on the CPU shim
+    (oracle/qwen_shim.cpp): prefill / step logits and greedy generate."""
+    _lib = None
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            lib = C.CDLL(REF_SO)
+            lib.ref_qwen_last_error.restype = C.c_char_p
+            lib.ref_qwen_load.restype = C.c_void_p
+            lib.ref_qwen_load.argtypes = [C.c_char_p]
+            lib.ref_qwen_free.argtypes = [C.c_void_p]
+            lib.ref_qwen_prefill.argtypes = [C.c_void_p, _U, C.c_size_t, _F]
+            lib.ref_qwen_step.argtypes = [C.c_void_p, C.c_uint32, _F]
+            lib.ref_qwen_generate.argtypes = [C.c_void_p, _U, C.c_size_t, C.c_uint32, _U, C.POINTER(C.c_uint32)]
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, bundle_dir: str):
+        self.h = self.lib().ref_qwen_load(bundle_dir.encode())
+        if not self.h:
+            raise OracleError(-2, self.lib().ref_qwen_last_error().decode())
+
+    def _check(self, rc):
+        if rc != 0:
+            raise OracleError(rc, self.lib().ref_qwen_last_error().decode())
+
+    def prefill(self, ids) -> np.ndarray:
+        i = np.ascontiguousarray(ids, np.uint32)
+        out = np.empty(QWEN_VOCAB, np.float32)
+        self._check(self.lib().ref_qwen_prefill(self.h, i, i.size, out))
+        return out
+
+    def step(self, token: int) -> np.ndarray:
+        out = np.empty(QWEN_VOCAB, np.float32)
+        self._check(self.lib().ref_qwen_step(self.h, token, out))
+        return out
+
+    def generate(self, ids, maximum: int = 1024) -> np.ndarray:
+        i = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros(max(1, maximum), np.uint32)
+        n = C.c_uint32()
+        self._check(self.lib().ref_qwen_generate(self.h, i, i.size, maximum, out, C.byref(n)))
+        return out[:n.value].copy()
+
+    def close(self):
+        if self.h:
+            self.lib().ref_qwen_free(self.h)
+            self.h = None
+
+
 def compare(actual, expected, tol=1e-4, rms_tol=1e-5):
     """The reference comparator (src/main.cpp:19-30): finite check, max_abs,
     mean_abs and RMSE; passes when max_abs < tol and rmse < rms_tol."""

@@ -39,6 +39,12 @@ Fixtures (all inputs seeded):
                      argmax), the distance of the top-p cumulative sums from
                      1 - top_p, and of the draw's uniform from the CDF
                      boundaries (decision_margins).
+  qwen.npz           the Qwen3-0.6B decoder (src/qwen.cpp) on a random-init
+                     bundle (seed 44, EOS row x 20 so greedy decoding ends):
+                     for two prompts, the prefill logits and three
+                     teacher-forced step logits at 4096 seeded positions plus
+                     the reference's top 64, greedy generate(128) ids, and the
+                     argmax gap (top-1 minus top-2 logit) of every selection.
   gpt_config1_philox.npz  configs[1] with the Philox4x32-10 stream (the
                      benchmark's mode, seed 1234): 1024 sampled codes from the
                      oracle port (the reference has only SplitMix64; the port
@@ -204,6 +210,58 @@ def make_margins(ref_path, out):
     print("wrote", out)
 
 
+QWEN_PROMPTS = {"a": (5, 24), "b": (11, 180)}  # name -> (seed, length); both reach EOS within 128
+
+
+def qwen_prompt(seed, n):
+    return np.random.default_rng(seed).integers(0, 151000, n).astype(np.uint32)
+
+
+def qwen_sample_index(logits, seed=9, n=4096):
+    """The logits a fixture keeps: n seeded positions and the top 64."""
+    idx = np.random.default_rng(seed).choice(logits.size, n, replace=False)
+    return np.unique(np.concatenate([idx, np.argsort(-logits.astype(np.float64), kind="stable")[:64]]))
+
+
+def make_qwen(out, eos_gain=20.0):
+    path = os.path.join(CACHE, "qwen_s44_g20")
+    sha = mit2.write_synthetic_qwen_bundle(path, seed=44, eos_gain=eos_gain)
+    ref = O.RefQwen(path)
+    d = {"bundle_seed": 44, "bundle_eos_gain": np.float32(eos_gain), "bundle_sha256": sha}
+    for name, (seed, n) in QWEN_PROMPTS.items():
+        ids = qwen_prompt(seed, n)
+        t = time.time()
+        lg = ref.prefill(ids)
+        idx = qwen_sample_index(lg)
+        d[f"{name}.ids"] = ids
+        d[f"{name}.prefill.index"] = idx.astype(np.uint32)
+        d[f"{name}.prefill.logits"] = lg[idx]
+        tok = int(np.argmax(lg))
+        for i in range(3):
+            lg = ref.step(tok)
+            idx = qwen_sample_index(lg, seed=10 + i)
+            d[f"{name}.step.{i}.input"] = np.uint32(tok)
+            d[f"{name}.step.{i}.index"] = idx.astype(np.uint32)
+            d[f"{name}.step.{i}.logits"] = lg[idx]
+            tok = int(np.argmax(lg))
+        gen = ref.generate(ids, 128)
+        d[f"{name}.generated"] = gen
+        # argmax gap of every selection, teacher-forced along the reference's ids
+        gaps = []
+        lg = ref.prefill(ids)
+        for i, g in enumerate(gen):
+            top = np.sort(lg.astype(np.float64))[-2:]
+            assert int(np.argmax(lg)) == int(g)
+            gaps.append(top[1] - top[0])
+            if i + 1 < len(gen):
+                lg = ref.step(int(g))
+        d[f"{name}.argmax_gap"] = np.array(gaps)
+        print("qwen", name, n, "generated", len(gen), "min gap %.2e" % min(gaps), time.time() - t, flush=True)
+    ref.close()
+    np.savez_compressed(out, **d)
+    print("wrote", out)
+
+
 def text_lengths(seed, n, lo=40, hi=300):
     """Text lengths of configs[2] requests, uniform in [lo, hi]."""
     return np.random.default_rng(seed).integers(lo, hi + 1, n)
@@ -329,7 +387,7 @@ def make_processors(out):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", choices=["full", "long", "margins", "processors", "config2_beam", "config2_batch",
-                                       "config3", "config1_philox", "codec"], default=None)
+                                       "config3", "config1_philox", "codec", "qwen"], default=None)
     ap.add_argument("--config2-codes", type=int, default=600)
     ap.add_argument("--long-codes", type=int, default=1024)
     a = ap.parse_args()
@@ -345,6 +403,8 @@ def main():
         make_long(path, sha, os.path.join(HERE, "gpt_long.npz"), a.long_codes)
     if a.only in (None, "codec"):
         make_codec(os.path.join(HERE, "codec.npz"))
+    if a.only in (None, "qwen"):
+        make_qwen(os.path.join(HERE, "qwen.npz"))
     if a.only in (None, "config3"):
         path, sha = bundle(42, 24, True)
         make_config3(path, sha, os.path.join(HERE, "gpt_config3.npz"))
