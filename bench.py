@@ -535,13 +535,107 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+QWEN_CPU_SCRIPT = r"""
+import json, sys, time
+sys.path.insert(0, {oracle!r})
+import numpy as np
+import oracle as O
+ref = O.RefQwen({bundle!r})
+ids = np.random.default_rng(5).integers(0, 151000, 24).astype(np.uint32)
+lg = ref.prefill(ids)
+tok = int(np.argmax(lg))
+t0 = time.perf_counter()
+for i in range({n}):
+    tok = int(np.argmax(ref.step(tok)))
+dt = time.perf_counter() - t0
+print(json.dumps({{"tokens_per_s": {n} / dt, "threads": O.RefOracle.threads()}}))
+"""
+
+
+def run_qwen(args):
+    """Qwen3-0.6B greedy decode, batch 1: the 180-id
+    prompt of tests/golden/qwen.npz (seed 11), generate(128) ending at EOS
+    after 70 ids.  value = decode steps per second of device time (the steps'
+    CUDA graphs); e2e = ids per second of the generate() call; roofline =
+    algorithmic bytes of a step (all layer weights, the tied head, the K/V
+    read) over the device time."""
+    import torch
+    if env_int("RANK", 0) != 0:
+        return
+    gpt = importlib.import_module("index-tts-25-metal_b200.gpt")
+    mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+    cache = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
+    path = os.path.join(cache, "qwen_s44_g20")
+    mit2.write_synthetic_qwen_bundle(path, seed=44, eos_gain=20.0)
+    dec = gpt.QwenDecoder(path, device=env_int("LOCAL_RANK", 0))
+    ids = np.random.default_rng(11).integers(0, 151000, 180).astype(np.uint32)
+    for _ in range(args.warmup):
+        dec.generate(ids, 128)
+    smi = ClockSampler(gpu_smi_id(env_int("LOCAL_RANK", 0)))
+    smi.start()
+    time.sleep(0.3)
+    dms, pms, steps, wall, n_ids = [], [], [], 0.0, 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        out = dec.generate(ids, 128)
+        wall += time.perf_counter() - t0
+        t = dec.last_timing()
+        dms.append(t.decode_ms)
+        pms.append(t.prefill_ms)
+        steps.append(int(t.steps))
+        n_ids += len(out)
+    clocks = smi.stop()
+    value = sum(steps) / (sum(dms) / 1000.0)
+    layer_bytes = 28 * (4096 * 1024 + 1024 * 2048 + 6144 * 1024 + 1024 * 3072) * 4
+    head_bytes = 151936 * 1024 * 4
+    n = steps[-1]
+    kv = sum(28 * 2 * 1024 * 4 * (ids.size + i + 1) for i in range(n))
+    alg = n * (layer_bytes + head_bytes) + kv
+    achieved = alg / (statistics.mean(dms) / 1000.0) / 1e9
+    pk, pk_kind = peaks()
+    cpu = None
+    if not args.no_cpu_baseline:
+        code = QWEN_CPU_SCRIPT.format(oracle=os.path.join(ROOT, "oracle"), bundle=path, n=16)
+        try:
+            r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+            j = json.loads(r.stdout.strip().splitlines()[-1])
+            cpu = {"value": j["tokens_per_s"], "unit": "tokens/s", "cores": j["threads"], "kind": "reference",
+                   "sample": "the reference's QwenDecoder (oracle/_ref) on the host: 16 greedy steps after a "
+                             "24-id prefill"}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"unavailable": str(e)[:200]}
+    line = {
+        "metric": "Qwen3-0.6B greedy decode tokens/s @B=1; % of HBM roofline", "value": value, "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(dms) / max(1, n), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init Qwen3-0.6B weights, EOS row x 20; seeded prompt ids)",
+        "config": {"workload": "Qwen3-0.6B emotion-text decoder: 180-id prompt, greedy generate(128) to EOS "
+                               f"({n + 1} ids)", "config": "qwen",
+                   "l2": "inputs larger than L2: each step streams 2.38 GB of fp32 weights"},
+        "e2e": {"value": n_ids / wall, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes),
+                "d2h_bytes_per_step": int(4 * (n + 1))},
+        "gpu_launches": int(n * (1 + 28 * 5 + 1) + 1 + 28 * 8 + 1),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": float(pk["hbm_gbs"]), "unit": "GB/s",
+                     "frac": achieved / float(pk["hbm_gbs"]), "traffic": None, "peak_source": f"{pk_kind} hbm_gbs",
+                     "kernel": "decode step graph (GEMVs, attention, head, argmax)",
+                     "algorithmic_bytes_per_launch": alg, "avg_launch_ms": statistics.mean(dms)},
+        "prefill": {"ms": statistics.mean(pms), "rows": int(ids.size), "gemm": "tcgen05 TF32 hi/lo (TMA-fed)"},
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    dec.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["0", "1", "2", "2beam", "3", "serving"], default="1",
+    ap.add_argument("--config", choices=["0", "1", "2", "2beam", "3", "serving", "qwen"], default="1",
                     help="BASELINE.json workload (1 = the headline)")
     ap.add_argument("--rows", type=int, default=16, help="rows in flight for --config serving")
     ap.add_argument("--cpu-tokens", type=int, default=48)
@@ -557,6 +651,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.config == "qwen":
+        run_qwen(args)
     else:
         run_ours(args)
 

@@ -216,6 +216,8 @@ void alloc_buffers(itts_qwen_ctx* c) {
     b.ids = c->alloc<uint32_t>(T, "prompt ids");
     b.out = c->alloc<uint32_t>(q::kMaxGenerate + 1, "selected ids");
     b.st = c->alloc<q::State>(1, "decode state");
+    b.cnt = c->alloc<int>(16, "arrival counters");
+    qck(cudaMemset(b.cnt, 0, 16 * 4), "arrival counters");
     b.status = c->alloc<int>(4, "status");
     qck(cudaMemset(b.status, 0, 16), "status");
     c->ws = c->alloc<float>(itts::tma_workspace_floats(), "GEMM workspace");

@@ -26,6 +26,7 @@
 // mit2_silu_mul_f32 (:363-374), mit2_gpt_argmax_f32 (:1269-1305, first index of
 // the maximum) and mit2_embedding_f32 (:281-294).
 #include <cmath>
+#include <utility>
 
 #include "common.cuh"
 #include "qwen.hpp"
@@ -263,114 +264,180 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* __restrict__ 
     }
 }
 
-// Decode attention, split K: CTA = (KV head j, chunk of 64 keys) computes for
-// query heads 2j and 2j + 1 the chunk's max, sum of exp and exp-weighted V
-// (K and V rows staged once for both heads).
-constexpr int kKLd = 132;
-constexpr size_t kAttnDecodeSmem = (64 * kKLd + 64 * kHeadDim + 2 * kHeadDim + 2 * 64) * sizeof(float);
+// ---- decode step --------------------------------------------------------
+// The decode kernels are launched with programmatic stream serialization
+// (PDL): each may start while its predecessor drains, does what does not
+// depend on it (the GEMVs load their weight rows), then waits for it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-__global__ void __launch_bounds__(128) k_attn_decode(const float* __restrict__ q, const float* __restrict__ kc,
-                                                     const float* __restrict__ vc, float* __restrict__ part,
-                                                     const State* st) {
-    extern __shared__ __align__(16) float smem[];
-    float* Ks = smem;                 // [64][kKLd]
-    float* Vs = Ks + 64 * kKLd;       // [64][128]
-    float* qs = Vs + 64 * kHeadDim;   // [2][128]
-    float* ps = qs + 2 * kHeadDim;    // [2][64]
-    __shared__ float red[2][4];
+// Decode attention of one step, with the q/k RMSNorm + RoPE of the step's
+// token and its K/V append folded in.  A fixed grid of CTAs walks the work
+// items (KV head j, chunk of 64 keys) of S = pos + 1 keys; an item computes
+// for query heads 2j and 2j + 1 the chunk's max, sum of exp and exp-weighted
+// V (K and V rows staged once for both heads), the chunk holding position pos
+// first writes the new K/V row.  The last item of a KV head to arrive (acq_rel
+// counter) merges the chunks of its two query heads in chunk order.
+constexpr int kKLd = 132;
+constexpr int kAttnCtas = 148;
+struct AttnSmem {
+    float Ks[64 * kKLd];
+    float Vs[64 * kHeadDim];
+    float qs[2 * kHeadDim];
+    float kn[kHeadDim];
+    float ps[2 * 64];
+    float red[8][2];
+    int last;
+};
+
+// RMSNorm (width 128, 128 threads of the calling group) and RoPE at `pos` of
+// vec -> dst (shared), as k_qk_norm_rope.
+__device__ __forceinline__ void norm_rope_128(const float* vec, const float* g, float* dst, float* red2, int pos,
+                                              int t, int bar) {
+    const float x = vec[t];
+    float ss = warp_sum(x * x);
+    if ((t & 31) == 0) red2[t >> 5] = ss;
+    asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+    ss = red2[0] + red2[1] + red2[2] + red2[3];
+    const float xn = x * (1.0f / sqrtf(ss / float(kHeadDim) + kEps)) * g[t];
+    dst[t] = xn;
+    asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+    const float angle = float(pos) * c_inv_freq[t & 63];
+    const float rot = t < 64 ? -dst[t + 64] : dst[t - 64];
+    const float r = xn * cosf(angle) + rot * sinf(angle);
+    asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+    dst[t] = r;
+}
+
+__global__ void __launch_bounds__(256) k_attn_step(float* __restrict__ qkv, const float* __restrict__ qn,
+                                                   const float* __restrict__ knw, float* __restrict__ kc,
+                                                   float* __restrict__ vc, float* __restrict__ part,
+                                                   int* __restrict__ cnt, float* __restrict__ out, const State* st) {
+    extern __shared__ __align__(16) unsigned char att_raw[];
+    AttnSmem& sm = *reinterpret_cast<AttnSmem*>(att_raw);
+    pdl_wait();
     if (finished(st)) return;
-    const int S = int(st->pos) + 1, j = blockIdx.x, c = blockIdx.y, k0 = c * 64;
-    if (k0 >= S) return;
-    const int n = min(64, S - k0), tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < 64 * 32; i += 128) {
-        const int r = i >> 5, c4 = i & 31;
-        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-        if (r < n) {
-            const size_t o = (size_t)(k0 + r) * kKvDim + j * kHeadDim + 4 * c4;
-            kv = *reinterpret_cast<const float4*>(kc + o);
-            vv = *reinterpret_cast<const float4*>(vc + o);
+    const int pos = int(st->pos), S = pos + 1, nch = (S + 63) / 64, items = kKvHeads * nch;
+    const int tid = threadIdx.x, half = tid >> 7, t = tid & 127, lane = tid & 31, warp = tid >> 5;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int j = it % kKvHeads, c = it / kKvHeads, k0 = c * 64, n = min(64, S - k0);
+        __syncthreads();  // the previous item's shared data is consumed
+        // query heads 2j (threads 0-127) and 2j + 1 (128-255), normalised and rotated
+        norm_rope_128(qkv + (2 * j + half) * kHeadDim, qn, sm.qs + half * kHeadDim, &sm.red[4 * half][0], pos, t,
+                      1 + half);
+        if (c == nch - 1) {  // this chunk holds position pos: append the step's K/V
+            if (half == 0) {
+                norm_rope_128(qkv + kQDim + j * kHeadDim, knw, sm.kn, &sm.red[0][1], pos, t, 1);
+                kc[(size_t)pos * kKvDim + j * kHeadDim + t] = sm.kn[t];
+            } else {
+                vc[(size_t)pos * kKvDim + j * kHeadDim + t] = qkv[kQDim + kKvDim + j * kHeadDim + t];
+            }
         }
-        *reinterpret_cast<float4*>(Ks + r * kKLd + 4 * c4) = kv;
-        *reinterpret_cast<float4*>(Vs + r * kHeadDim + 4 * c4) = vv;
-    }
-    qs[tid] = q[(2 * j) * kHeadDim + tid];
-    qs[kHeadDim + tid] = q[(2 * j + 1) * kHeadDim + tid];
-    __syncthreads();
-    const int key = tid & 63, hh = tid >> 6;  // warps 0-1: head 2j, warps 2-3: head 2j + 1
-    float s = -INFINITY;
-    if (key < n) {
+        __syncthreads();  // the appended row is visible to the CTA
+        for (int i = tid; i < 64 * 32; i += 256) {
+            const int r = i >> 5, c4 = i & 31;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (r < n) {
+                const size_t o = (size_t)(k0 + r) * kKvDim + j * kHeadDim + 4 * c4;
+                kv = __ldcg(reinterpret_cast<const float4*>(kc + o));
+                vv = __ldcg(reinterpret_cast<const float4*>(vc + o));
+            }
+            *reinterpret_cast<float4*>(sm.Ks + r * kKLd + 4 * c4) = kv;
+            *reinterpret_cast<float4*>(sm.Vs + r * kHeadDim + 4 * c4) = vv;
+        }
+        __syncthreads();
+        // scores: thread (head = half, key = t >> 1, dims (t & 1) * 64 ..)
+        const int key = t >> 1, dh = (t & 1) * 64;
         float acc = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < kHeadDim; d += 4) {
-            const float4 kv = *reinterpret_cast<const float4*>(Ks + key * kKLd + d);
-            const float4 qv = *reinterpret_cast<const float4*>(qs + hh * kHeadDim + d);
+#pragma unroll 4
+        for (int d = 0; d < 64; d += 4) {
+            const float4 kv = *reinterpret_cast<const float4*>(sm.Ks + key * kKLd + dh + d);
+            const float4 qv = *reinterpret_cast<const float4*>(sm.qs + half * kHeadDim + dh + d);
             acc = fmaf(qv.x, kv.x, acc);
             acc = fmaf(qv.y, kv.y, acc);
             acc = fmaf(qv.z, kv.z, acc);
             acc = fmaf(qv.w, kv.w, acc);
         }
-        s = acc * kScale;
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        const float s = key < n ? acc * kScale : -INFINITY;
+        float mx = warp_max(s);
+        if (lane == 0) sm.red[warp][0] = mx;
+        __syncthreads();
+        mx = fmaxf(fmaxf(sm.red[4 * half][0], sm.red[4 * half + 1][0]), fmaxf(sm.red[4 * half + 2][0], sm.red[4 * half + 3][0]));
+        const float p = key < n ? expf(s - mx) : 0.f;
+        if ((t & 1) == 0) sm.ps[half * 64 + key] = p;
+        const float ls = warp_sum((t & 1) == 0 ? p : 0.f);
+        if (lane == 0) sm.red[warp][1] = ls;
+        __syncthreads();
+        const float l = sm.red[4 * half][1] + sm.red[4 * half + 1][1] + sm.red[4 * half + 2][1] + sm.red[4 * half + 3][1];
+        float o = 0.f;
+        for (int k = 0; k < n; ++k) o = fmaf(sm.ps[half * 64 + k], sm.Vs[k * kHeadDim + t], o);
+        float* pp = part + ((size_t)(2 * j + half) * kMaxChunks + c) * kPartStride;
+        pp[2 + t] = o;
+        if (t == 0) {
+            pp[0] = mx;
+            pp[1] = l;
+        }
+        // arrival per KV head; the last of its nch items merges heads 2j, 2j + 1
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            int prev;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt + j) : "memory");
+            sm.last = prev == nch - 1;
+            if (sm.last) cnt[j] = 0;
+        }
+        __syncthreads();
+        if (sm.last) {
+            const float* ph = part + (size_t)(2 * j + half) * kMaxChunks * kPartStride;
+            float M = -INFINITY;
+            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(ph + cc * kPartStride));
+            float L = 0.f, acco = 0.f;
+            for (int cc = 0; cc < nch; ++cc) {
+                const float w = expf(__ldcg(ph + cc * kPartStride) - M);
+                L = fmaf(__ldcg(ph + cc * kPartStride + 1), w, L);
+                acco = fmaf(__ldcg(ph + cc * kPartStride + 2 + t), w, acco);
+            }
+            out[(2 * j + half) * kHeadDim + t] = acco / L;
+        }
     }
-    float mx = warp_max(s);
-    if (lane == 0) red[0][warp] = mx;
-    __syncthreads();
-    mx = fmaxf(red[0][2 * hh], red[0][2 * hh + 1]);
-    const float p = key < n ? expf(s - mx) : 0.f;
-    const float ls = warp_sum(p);
-    if (lane == 0) red[1][warp] = ls;
-    ps[hh * 64 + key] = p;
-    __syncthreads();
-    const float l0 = red[1][0] + red[1][1], l1 = red[1][2] + red[1][3];
-    const float m0 = fmaxf(red[0][0], red[0][1]), m1 = fmaxf(red[0][2], red[0][3]);
-    float o0 = 0.f, o1 = 0.f;
-    for (int k = 0; k < n; ++k) {
-        const float v = Vs[k * kHeadDim + tid];
-        o0 = fmaf(ps[k], v, o0);
-        o1 = fmaf(ps[64 + k], v, o1);
-    }
-    float* p0 = part + ((size_t)(2 * j) * kMaxChunks + c) * kPartStride;
-    float* p1 = part + ((size_t)(2 * j + 1) * kMaxChunks + c) * kPartStride;
-    p0[2 + tid] = o0;
-    p1[2 + tid] = o1;
-    if (tid == 0) {
-        p0[0] = m0;
-        p0[1] = l0;
-        p1[0] = m1;
-        p1[1] = l1;
-    }
-}
-
-// Merge of a query head's chunk partials: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c.
-__global__ void __launch_bounds__(128) k_attn_merge(const float* __restrict__ part, float* __restrict__ out,
-                                                    const State* st) {
-    if (finished(st)) return;
-    const int h = blockIdx.x, d = threadIdx.x, nch = (int(st->pos) + 1 + 63) / 64;
-    const float* p = part + (size_t)h * kMaxChunks * kPartStride;
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, p[c * kPartStride]);
-    float L = 0.f, o = 0.f;
-    for (int c = 0; c < nch; ++c) {
-        const float w = expf(p[c * kPartStride] - M);
-        L = fmaf(p[c * kPartStride + 1], w, L);
-        o = fmaf(p[c * kPartStride + 2 + d], w, o);
-    }
-    out[h * kHeadDim + d] = o / L;
+    pdl_trigger();
 }
 
 // Decode GEMVs y = W x over rows of K floats, one warp per row (SwiGLU: per
 // gate / up row pair), kGemvRows rows per CTA; x staged in shared memory,
-// optionally RMS-normalised with gamma first (width 1024).
+// optionally RMS-normalised with gamma first (width 1024).  The weight rows
+// are loaded before the wait for the predecessor.  kGemvHead (the tied head)
+// also reduces the CTA's (value, index) maximum, and the last CTA to arrive
+// takes the argmax over all of them (the first index of the maximum) and
+// advances the State: the selected id is appended to out and becomes the next
+// step's input (at the next position when `advance`); EOS or a spent budget
+// ends the run.
 enum GemvEpi : int { kGemvPlain = 0, kGemvResid = 1, kGemvSwiGLU = 2, kGemvHead = 3 };
 
 template <int K, int EPI, bool NORM>
 __global__ void __launch_bounds__(256) k_gemv(const float* __restrict__ W, const float* __restrict__ x,
                                               const float* __restrict__ gamma, float* __restrict__ y,
-                                              float* __restrict__ best, const State* st) {
+                                              float* __restrict__ best, int* __restrict__ cnt,
+                                              uint32_t* __restrict__ out, State* st, int advance) {
     __shared__ __align__(16) float xs[K];
     __shared__ float red[8];
-    __shared__ float bv[kGemvRows];
-    if (finished(st)) return;
+    __shared__ float bv[32];
+    __shared__ uint32_t bi[32];
+    __shared__ int last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int kIt = K / 128;  // float4 per lane
+    constexpr int kRows = EPI == kGemvSwiGLU ? 2 : 1;
+    const size_t row0 = ((size_t)blockIdx.x * kGemvRows + warp) * kRows;
+    float4 wv[kRows][kIt];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+        const float4* wr = reinterpret_cast<const float4*>(W + (row0 + r) * K);
+#pragma unroll
+        for (int i = 0; i < kIt; ++i) wv[r][i] = ld_stream(wr + lane + 32 * i);
+    }
+    pdl_wait();
+    if (advance && finished(st)) return;
     for (int i = 4 * tid; i < K; i += 1024) *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
     if (NORM) {
         static_assert(!NORM || K == kDim, "RMSNorm prologue is 1024 wide");
@@ -382,64 +449,56 @@ __global__ void __launch_bounds__(256) k_gemv(const float* __restrict__ W, const
         reinterpret_cast<float4*>(xs)[tid] = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
     }
     __syncthreads();
-    constexpr int kIt = K / 128;  // float4 per lane
-    constexpr int kRows = EPI == kGemvSwiGLU ? 2 : 1;
     float d[kRows];
-    const size_t row0 = ((size_t)blockIdx.x * kGemvRows + warp) * kRows;
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
-        const float4* wr = reinterpret_cast<const float4*>(W + (row0 + r) * K);
-        float4 wv[kIt];
-#pragma unroll
-        for (int i = 0; i < kIt; ++i) wv[i] = ld_stream(wr + lane + 32 * i);
         float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int i = 0; i < kIt; ++i) {
             const float4 xv = reinterpret_cast<const float4*>(xs)[lane + 32 * i];
-            a0 = fmaf(wv[i].x, xv.x, a0);
-            a1 = fmaf(wv[i].y, xv.y, a1);
-            a0 = fmaf(wv[i].z, xv.z, a0);
-            a1 = fmaf(wv[i].w, xv.w, a1);
+            a0 = fmaf(wv[r][i].x, xv.x, a0);
+            a1 = fmaf(wv[r][i].y, xv.y, a1);
+            a0 = fmaf(wv[r][i].z, xv.z, a0);
+            a1 = fmaf(wv[r][i].w, xv.w, a1);
         }
         d[r] = warp_sum(a0 + a1);
     }
-    if (EPI == kGemvHead) {
+    pdl_trigger();
+    if (EPI != kGemvHead) {
         if (lane == 0) {
-            y[row0] = d[0];
-            bv[warp] = d[0];
+            if (EPI == kGemvPlain) y[row0] = d[0];
+            if (EPI == kGemvResid) y[row0] += d[0];
+            if (EPI == kGemvSwiGLU) y[row0 / 2] = d[0] / (1.0f + expf(-d[0])) * d[1];
         }
-        __syncthreads();
-        if (tid == 0) {  // first index of the CTA's maximum
-            int bi = 0;
-            for (int i = 1; i < kGemvRows; ++i)
-                if (bv[i] > bv[bi]) bi = i;
-            best[2 * blockIdx.x] = bv[bi];
-            best[2 * blockIdx.x + 1] = __uint_as_float(uint32_t(blockIdx.x * kGemvRows + bi));
-        }
-    } else if (lane == 0) {
-        if (EPI == kGemvPlain) y[row0] = d[0];
-        if (EPI == kGemvResid) y[row0] += d[0];
-        if (EPI == kGemvSwiGLU) y[row0 / 2] = d[0] / (1.0f + expf(-d[0])) * d[1];
+        return;
     }
-}
-
-// Argmax over the head CTAs' (value, index) pairs (the first index of the
-// maximum), then the State advances: the selected id is appended to out and
-// becomes the next step's input (at the next position when `advance`); EOS or a
-// spent budget ends the run.
-__global__ void __launch_bounds__(1024) k_argmax_final(const float* __restrict__ best, uint32_t* __restrict__ out,
-                                                       State* st, int advance) {
-    __shared__ float sv[32];
-    __shared__ uint32_t si[32];
-    if (finished(st)) return;
+    if (lane == 0) {
+        y[row0] = d[0];
+        bv[warp] = d[0];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int b = 0;
+        for (int i = 1; i < kGemvRows; ++i)
+            if (bv[i] > bv[b]) b = i;
+        best[2 * blockIdx.x] = bv[b];
+        best[2 * blockIdx.x + 1] = __uint_as_float(uint32_t(blockIdx.x * kGemvRows + b));
+        __threadfence();
+        int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+        last = prev == int(gridDim.x) - 1;
+        if (last) *cnt = 0;
+    }
+    __syncthreads();
+    if (!last) return;
     float v = -INFINITY;
     uint32_t idx = 0xffffffffu;
-    for (int i = threadIdx.x; i < kHeadCtas; i += 1024) {
-        const float bvv = best[2 * i];
-        const uint32_t bi = __float_as_uint(best[2 * i + 1]);
-        if (bvv > v || (bvv == v && bi < idx)) {
-            v = bvv;
-            idx = bi;
+    for (int i = tid; i < int(gridDim.x); i += 256) {
+        const float b = __ldcg(best + 2 * i);
+        const uint32_t ii = __float_as_uint(__ldcg(best + 2 * i + 1));
+        if (b > v || (b == v && ii < idx)) {
+            v = b;
+            idx = ii;
         }
     }
 #pragma unroll
@@ -451,17 +510,16 @@ __global__ void __launch_bounds__(1024) k_argmax_final(const float* __restrict__
             idx = oi;
         }
     }
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
-        sv[w] = v;
-        si[w] = idx;
+        bv[warp] = v;
+        bi[warp] = idx;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int i = 1; i < 32; ++i)
-            if (sv[i] > v || (sv[i] == v && si[i] < idx)) {
-                v = sv[i];
-                idx = si[i];
+    if (tid == 0) {
+        for (int i = 1; i < 8; ++i)
+            if (bv[i] > v || (bv[i] == v && bi[i] < idx)) {
+                v = bv[i];
+                idx = bi[i];
             }
         if (idx >= uint32_t(kVocab)) idx = 0;  // no finite logit: the reference's initial index
         const uint32_t n = st->n_out;
@@ -473,6 +531,14 @@ __global__ void __launch_bounds__(1024) k_argmax_final(const float* __restrict__
     }
 }
 
+__global__ void __launch_bounds__(256) k_embed_step(const float* __restrict__ table, float* __restrict__ out,
+                                                    const State* st) {
+    pdl_wait();
+    if (finished(st)) return;
+    reinterpret_cast<float4*>(out)[threadIdx.x] = reinterpret_cast<const float4*>(table + (size_t)st->token * kDim)[threadIdx.x];
+    pdl_trigger();
+}
+
 __global__ void k_interleave_rows(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
                                   int rows, int cols) {
     const size_t n = (size_t)rows * cols;
@@ -482,12 +548,28 @@ __global__ void k_interleave_rows(const float* __restrict__ a, const float* __re
     }
 }
 
+// Launch with programmatic stream serialization (captured as a programmatic
+// edge inside the decode-step graph).
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kernel)(P...), int grid, int block, size_t smem, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+
 template <int K, int EPI, bool NORM>
-cudaError_t gemv(const float* W, const float* x, const float* gamma, float* y, float* best, int rows, const State* st,
-                 cudaStream_t s) {
+cudaError_t gemv(const float* W, const float* x, const float* gamma, float* y, float* best, int* cnt, uint32_t* out,
+                 State* st, int advance, int rows, cudaStream_t s) {
     const int per = kGemvRows * (EPI == kGemvSwiGLU ? 2 : 1);
-    k_gemv<K, EPI, NORM><<<rows / per, 256, 0, s>>>(W, x, gamma, y, best, st);
-    return cudaGetLastError();
+    return launch_pdl(k_gemv<K, EPI, NORM>, rows / per, 256, 0, s, W, x, gamma, y, best, cnt, out, st, advance);
 }
 
 float* layer_k(const Buffers& b, int layer) { return b.kv + (size_t)layer * 2 * kCap * kKvDim; }
@@ -501,14 +583,20 @@ cudaError_t init_tables() {
     return cudaMemcpyToSymbol(c_inv_freq, f, sizeof f);
 }
 
+cudaError_t prepare_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kAttnPrefillSmem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_attn_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem));
+}
+
 cudaError_t launch_embed(const Weights& w, const Buffers& b, int T, cudaStream_t s) {
     k_embed<<<T, 256, 0, s>>>(w.embed, b.ids, b.hidden, nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t launch_decode_embed(const Weights& w, const Buffers& b, cudaStream_t s) {
-    k_embed<<<1, 256, 0, s>>>(w.embed, nullptr, b.hidden, b.st);
-    return cudaGetLastError();
+    return launch_pdl(k_embed_step, 1, 256, 0, s, w.embed, b.hidden, (const State*)b.st);
 }
 
 cudaError_t launch_rmsnorm_split(const float* x, const float* g, float* hi, float* lo, int T, cudaStream_t s) {
@@ -522,13 +610,6 @@ cudaError_t launch_qk_norm_rope(const LayerW& L, const Buffers& b, int layer, in
     return cudaGetLastError();
 }
 
-cudaError_t prepare_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kAttnPrefillSmem);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnDecodeSmem);
-}
-
 cudaError_t launch_attn_prefill(const Buffers& b, int layer, int T, cudaStream_t s) {
     k_attn_prefill<<<dim3(kQHeads, (T + 63) / 64), 256, kAttnPrefillSmem, s>>>(b.qkv, layer_k(b, layer),
                                                                                layer_v(b, layer), b.att_hi, b.att_lo,
@@ -538,30 +619,28 @@ cudaError_t launch_attn_prefill(const Buffers& b, int layer, int T, cudaStream_t
 
 cudaError_t launch_decode_layer(const LayerW& L, const Buffers& b, int layer, cudaStream_t s) {
     cudaError_t e;
-    if ((e = gemv<kDim, kGemvPlain, true>(L.w_qkv, b.hidden, L.ln1, b.qkv, nullptr, kQkv, b.st, s)) != cudaSuccess)
+    if ((e = gemv<kDim, kGemvPlain, true>(L.w_qkv, b.hidden, L.ln1, b.qkv, nullptr, nullptr, nullptr, b.st, 1, kQkv,
+                                          s)) != cudaSuccess)
         return e;
-    if ((e = launch_qk_norm_rope(L, b, layer, 1, true, s)) != cudaSuccess) return e;
-    k_attn_decode<<<dim3(kKvHeads, kMaxChunks), 128, kAttnDecodeSmem, s>>>(b.qkv, layer_k(b, layer),
-                                                                           layer_v(b, layer), b.part, b.st);
-    k_attn_merge<<<kQHeads, 128, 0, s>>>(b.part, b.att_hi, b.st);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if ((e = gemv<kQDim, kGemvResid, false>(L.w_o, b.att_hi, nullptr, b.hidden, nullptr, kDim, b.st, s)) != cudaSuccess)
+    if ((e = launch_pdl(k_attn_step, kAttnCtas, 256, sizeof(AttnSmem), s, b.qkv, L.qn, L.kn, layer_k(b, layer),
+                        layer_v(b, layer), b.part, b.cnt, b.att_hi, (const State*)b.st)) != cudaSuccess)
         return e;
-    if ((e = gemv<kDim, kGemvSwiGLU, true>(L.w_gu, b.hidden, L.ln2, b.gu_hi, nullptr, 2 * kFfn, b.st, s)) !=
-        cudaSuccess)
+    if ((e = gemv<kQDim, kGemvResid, false>(L.w_o, b.att_hi, nullptr, b.hidden, nullptr, nullptr, nullptr, b.st, 1,
+                                            kDim, s)) != cudaSuccess)
         return e;
-    return gemv<kFfn, kGemvResid, false>(L.w_down, b.gu_hi, nullptr, b.hidden, nullptr, kDim, b.st, s);
+    if ((e = gemv<kDim, kGemvSwiGLU, true>(L.w_gu, b.hidden, L.ln2, b.gu_hi, nullptr, nullptr, nullptr, b.st, 1,
+                                           2 * kFfn, s)) != cudaSuccess)
+        return e;
+    return gemv<kFfn, kGemvResid, false>(L.w_down, b.gu_hi, nullptr, b.hidden, nullptr, nullptr, nullptr, b.st, 1,
+                                         kDim, s);
 }
 
-// Final RMSNorm of `last_row` fused into the tied head, then the argmax, which
-// sets the State (a decode step also moves its position on; after a prefill
-// the host has set the position to the prompt's length).
+// Final RMSNorm of `last_row` fused into the tied head; its last CTA takes the
+// argmax and sets the State (a decode step also moves its position on; after
+// a prefill the host has set the position to the prompt's length).
 cudaError_t launch_head(const Weights& w, const Buffers& b, const float* last_row, bool decode, cudaStream_t s) {
-    cudaError_t e = gemv<kDim, kGemvHead, true>(w.embed, last_row, w.norm, b.logits, b.best, kVocab,
-                                                decode ? b.st : nullptr, s);
-    if (e != cudaSuccess) return e;
-    k_argmax_final<<<1, 1024, 0, s>>>(b.best, b.out, b.st, decode ? 1 : 0);
-    return cudaGetLastError();
+    return gemv<kDim, kGemvHead, true>(w.embed, last_row, w.norm, b.logits, b.best, b.cnt + kKvHeads, b.out, b.st,
+                                       decode ? 1 : 0, kVocab, s);
 }
 
 cudaError_t launch_interleave_rows(const float* a, const float* b, float* out, int rows, int cols, cudaStream_t s) {

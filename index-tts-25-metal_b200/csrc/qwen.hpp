@@ -69,6 +69,7 @@ struct Buffers {
     uint32_t* ids;   // [kMaxPrompt] prompt ids
     uint32_t* out;   // [kMaxGenerate] selected ids
     State* st;
+    int* cnt;        // arrival counters: [0, 8) attention per KV head, [8] head GEMV (the last arriver resets)
     int* status;
 };
 
