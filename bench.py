@@ -522,8 +522,7 @@ def run_ours(args):
                          "forward_steps_per_launch": fwd_steps[-1]},
             "prefill_ms": statistics.mean(prefill_ms),
             "prefill": {"ms": statistics.mean(prefill_ms),
-                        "gemm": "tcgen05 TF32 hi/lo, three products (TMA-fed)" if not wb
-                        else "tcgen05 TF32 hi/lo (register-staged, bf16 weights)",
+                        "gemm": "tcgen05 TF32 hi/lo, three products (TMA-fed)" + (", bf16 weights widened" if wb else ""),
                         "cuda_core_fp32_ms": cuda_core_prefill_ms},
             "clocks": clocks,
         }

@@ -492,6 +492,15 @@ __global__ void k_split_tf32(const float* __restrict__ w, float* __restrict__ hi
     }
 }
 
+// bf16 W -> fp32 (the bf16 value is the high half of the fp32 word; exact in TF32).
+__global__ void k_widen_bf16(const uint16_t* __restrict__ w, float* __restrict__ out, size_t n4) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const uint2 raw = reinterpret_cast<const uint2*>(w)[i];
+        reinterpret_cast<float4*>(out)[i] = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                                                         __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+    }
+}
+
 // ---- host side ----------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -567,11 +576,17 @@ int sm_count() {
 
 }  // namespace
 
-cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, cudaStream_t s) {
+cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, bool wbf16, cudaStream_t s) {
     if (!encode_fn()) return cudaErrorNotSupported;
     p->layers = hw.layers;
-    cudaError_t e = cudaMalloc(&p->wsplit, mat_offset(hw.layers, 0) * sizeof(float));
+    // fp32 weights: hi and lo per matrix.  bf16 weights are exact in TF32:
+    // hi is the widened matrix, and every lo map reads one shared zero matrix.
+    const size_t zero_floats = size_t(kFfn) * kWidth;
+    const size_t wfloats = wbf16 ? mat_offset(hw.layers, 0) / 2 + zero_floats : mat_offset(hw.layers, 0);
+    cudaError_t e = cudaMalloc(&p->wsplit, wfloats * sizeof(float));
     if (e != cudaSuccess) return e;
+    float* zero = p->wsplit + (wfloats - zero_floats);
+    if (wbf16 && (e = cudaMemsetAsync(zero, 0, zero_floats * sizeof(float), s)) != cudaSuccess) return e;
     const size_t act = size_t(kMaxPrefix) * (4 * kWidth + 2 * kFfn);
     float* a = nullptr;
     if ((e = cudaMalloc(&a, act * sizeof(float))) != cudaSuccess) return e;
@@ -591,9 +606,12 @@ cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, cudaStream_t s) {
         const float* src[4] = {L.w_qkv, L.w_o, L.w_fc, L.w_mp};
         for (int mat = 0; mat < 4; ++mat) {
             const size_t n = size_t(kMatN[mat]) * kMatK[mat];
-            float* hi = p->wsplit + mat_offset(l, mat);
-            float* lo = hi + n;
-            k_split_tf32<<<592, 256, 0, s>>>(src[mat], hi, lo, n / 4);
+            float* hi = p->wsplit + (wbf16 ? mat_offset(l, mat) / 2 : mat_offset(l, mat));
+            float* lo = wbf16 ? zero : hi + n;
+            if (wbf16)
+                k_widen_bf16<<<592, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(src[mat]), hi, n / 4);
+            else
+                k_split_tf32<<<592, 256, 0, s>>>(src[mat], hi, lo, n / 4);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             if ((e = make_map(&wmaps(p)[(l * 4 + mat) * 2], hi, kMatN[mat], kMatK[mat])) != cudaSuccess) return e;
             if ((e = make_map(&wmaps(p)[(l * 4 + mat) * 2 + 1], lo, kMatN[mat], kMatK[mat])) != cudaSuccess) return e;

@@ -73,8 +73,8 @@ struct itts_gpt_state {
 
 struct itts_gpt_ctx {
     int device = 0, dtype = 0, sm_count = 0, mode = 0;
-    int prefill_mode = 0;           // 0: tensor-core GEMMs, 1: CUDA-core fp32 tiles (fp32 weights)
-    itts::TmaPrefill tma{};         // fp32 weights: TF32-split weights and activations of the tensor-core prefill
+    int prefill_mode = 0;           // 0: tensor-core GEMMs, 1: CUDA-core fp32 tiles
+    itts::TmaPrefill tma{};         // TF32-split weights and activations of the tensor-core prefill
     cudaStream_t stream = nullptr;
     std::string err;
     uint32_t layers = 0, mel_pos_rows = 0, text_pos_rows = 0;
@@ -414,10 +414,8 @@ void launch_decode(itts_gpt_ctx* c, const itts::DecodeArgs& a) {
     }
 }
 
-// The tensor-core prefill state of an fp32 context in prefill mode 0, else null.
-itts::TmaPrefill* tma_of(itts_gpt_ctx* c) {
-    return c->dtype == ITTS_WEIGHTS_F32 && c->prefill_mode == 0 && c->tma.wsplit ? &c->tma : nullptr;
-}
+// The tensor-core prefill state in prefill mode 0, else null.
+itts::TmaPrefill* tma_of(itts_gpt_ctx* c) { return c->prefill_mode == 0 && c->tma.wsplit ? &c->tma : nullptr; }
 
 // prefix already in d_hidden
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
@@ -1093,8 +1091,8 @@ int itts_gpt_create(const char* bundle_dir, int device, int weight_dtype, itts_g
         for (cudaEvent_t& e : c->ev) ck(cudaEventCreate(&e), "event creation");
         upload_weights(c.get(), bundle);
         alloc_buffers(c.get());
-        if (weight_dtype == ITTS_WEIGHTS_F32)
-            ck(itts::tma_prefill_init(&c->tma, c->hw, c->stream), "tensor-core prefill setup");
+        ck(itts::tma_prefill_init(&c->tma, c->hw, weight_dtype == ITTS_WEIGHTS_BF16, c->stream),
+           "tensor-core prefill setup");
         ck(cudaDeviceSynchronize(), "load");
     }, /*set_device=*/false);
     if (rc != ITTS_OK) {

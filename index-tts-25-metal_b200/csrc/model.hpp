@@ -186,10 +186,11 @@ cudaError_t launch_batch_sample(const BatchArgs& a, cudaStream_t s);
 cudaError_t launch_beam_scores(const float* logits, const SampleOpts& o, const uint32_t* hist, uint32_t hist_n,
                                float beam_score, float* tmp, float* out, int* status, cudaStream_t s);
 
-// Tensor-core prefill of the fp32-weight path (gemm_tma.cu).  Every GEMM
-// operand is held as two TF32-exact fp32 arrays, hi = x rounded to TF32 and
-// lo = (x - hi) rounded to TF32: the weights split once when the context is
-// created, the activations by the kernel that produces them.  `maps` holds the
+// Tensor-core prefill (gemm_tma.cu).  Every GEMM operand is held as two
+// TF32-exact fp32 arrays, hi = x rounded to TF32 and lo = (x - hi) rounded to
+// TF32: the weights split once when the context is created (bf16 weights are
+// exact in TF32: hi is the widened matrix, lo a zero matrix), the activations
+// by the kernel that produces them.  `maps` holds the
 // TMA tensor maps of the split weights (host memory, encoded once).
 enum TmaMatrix : int { kMatQkv = 0, kMatO = 1, kMatFc = 2, kMatMp = 3 };
 struct TmaPrefill {
@@ -205,7 +206,7 @@ struct TmaPrefill {
     int act_rows = -1;                           // rows the activation maps were encoded for
     alignas(64) unsigned char act_maps[6][128];  // x, att, ff (hi, lo) tensor maps for act_rows (64-byte aligned)
 };
-cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, cudaStream_t s);
+cudaError_t tma_prefill_init(TmaPrefill* p, const ModelW& hw, bool wbf16, cudaStream_t s);
 
 // The same GEMM for other models (gemm_tma.cu): C = epi(A W^T + bias), A
 // [M][K] and W [N][K] each given by the tensor maps of its TF32 hi and lo
@@ -250,7 +251,7 @@ struct PrefillArgs {
     int T;
     bool wbf16;   // matrices stored bf16
     int* status;  // device status word (bounded waits of the tensor-core GEMM)
-    TmaPrefill* tma;  // fp32 weights on the TMA-fed tensor-core GEMM; null: CUDA-core tiles
+    TmaPrefill* tma;  // the TMA-fed tensor-core GEMM; null: CUDA-core tiles
 };
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
 

@@ -324,22 +324,14 @@ static cudaError_t launch_attn(const float* qkv, float* out, float* out_lo, int 
     return cudaGetLastError();
 }
 
-bool gemm_tc_supported(int N, int K);
-cudaError_t launch_gemm_tc(int epi, bool wbf16, const float* A, const void* W, const float* bias, const float* R,
-                           float* C, int M, int N, int K, int* status, cudaStream_t s);
 cudaError_t launch_gemm_tma(TmaPrefill* p, int layer, int mat, const float* bias, const float* R, float* C,
                             float* C_lo, int M, int* status, cudaStream_t s);
 
-// bf16 weights: the register-staged tensor-core GEMM (gemm_tc.cu, three TF32
-// products).  fp32 weights without a TmaPrefill: the CUDA-core tiles above.
+// Prefill mode 1: the CUDA-core tiles above (fp32 or bf16 weights).
 static_assert(kWidth % 32 == 0 && kFfn % 32 == 0, "k_gemm_nt k-tiles of 32");
 template <int EPI>
 static void gemm(const float* A, const float* W, bool wb, const float* bias, const float* R, float* C, int M, int N,
-                 int K, int* status, cudaStream_t s) {
-    if (wb && gemm_tc_supported(N, K)) {
-        launch_gemm_tc(EPI, wb, A, W, bias, R, C, M, N, K, status, s);
-        return;
-    }
+                 int K, cudaStream_t s) {
     dim3 grid((N + 63) / 64, (M + 63) / 64);
     if (wb)
         k_gemm_nt<EPI, true><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
@@ -347,7 +339,7 @@ static void gemm(const float* A, const float* W, bool wb, const float* bias, con
         k_gemm_nt<EPI, false><<<grid, 256, 0, s>>>(A, W, bias, R, C, M, N, K);
 }
 
-// fp32 weights on the TMA-fed tensor-core GEMM (gemm_tma.cu): the operands of
+// Prefill mode 0: the TMA-fed tensor-core GEMM (gemm_tma.cu); the operands of
 // every GEMM are split into TF32 hi / lo by the kernel that produces them.
 static cudaError_t prefill_layers_tma(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
     const int T = p.T;
@@ -376,19 +368,19 @@ static cudaError_t prefill_layers_tma(const PrefillArgs& p, cudaStream_t s, uint
 }
 
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
-    if (p.tma && !p.wbf16) return prefill_layers_tma(p, s, launches);
+    if (p.tma) return prefill_layers_tma(p, s, launches);
     const int T = p.T;
     for (int l = 0; l < p.hw->layers; ++l) {
         const LayerW& L = p.hw->layer[l];
         k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, p.x, nullptr);
-        gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, p.status, s);
+        gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, s);
         k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
             p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
         if (cudaError_t e = launch_attn(p.qkv, p.att, nullptr, T, s); e != cudaSuccess) return e;
-        gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, p.status, s);
+        gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, s);
         k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x, nullptr);
-        gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, p.status, s);
-        gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, p.status, s);
+        gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, s);
+        gemm<kEpiResid>(p.ff, L.w_mp, p.wbf16, L.b_mp, p.r, p.hidden, T, kWidth, kFfn, s);
         *launches += 8;
     }
     return cudaGetLastError();
