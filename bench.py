@@ -552,7 +552,7 @@ print(json.dumps({{"tokens_per_s": {n} / dt, "threads": O.RefOracle.threads()}})
 
 
 def run_qwen(args):
-    """Qwen3-0.6B greedy decode, batch 1: the 180-id
+    """Qwen3-0.6B greedy decode (the emotion-text model, src/qwen.cpp), batch 1: the 180-id
     prompt of tests/golden/qwen.npz (seed 11), generate(128) ending at EOS
     after 70 ids.  value = decode steps per second of device time (the steps'
     CUDA graphs); e2e = ids per second of the generate() call; roofline =
