@@ -321,29 +321,41 @@ __global__ void __launch_bounds__(256) k_attn_step(float* __restrict__ qkv, cons
     const int tid = threadIdx.x, half = tid >> 7, t = tid & 127, lane = tid & 31, warp = tid >> 5;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
         const int j = it % kKvHeads, c = it / kKvHeads, k0 = c * 64, n = min(64, S - k0);
+        // the chunk's cached K/V rows (all but position pos) go into registers
+        // first, so their latency overlaps the norm / RoPE work below
+        float4 kr[8], vr[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * u, r = i >> 5, c4 = i & 31;
+            kr[u] = vr[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < n && k0 + r != pos) {
+                const size_t o = (size_t)(k0 + r) * kKvDim + j * kHeadDim + 4 * c4;
+                kr[u] = __ldcg(reinterpret_cast<const float4*>(kc + o));
+                vr[u] = __ldcg(reinterpret_cast<const float4*>(vc + o));
+            }
+        }
         __syncthreads();  // the previous item's shared data is consumed
         // query heads 2j (threads 0-127) and 2j + 1 (128-255), normalised and rotated
         norm_rope_128(qkv + (2 * j + half) * kHeadDim, qn, sm.qs + half * kHeadDim, &sm.red[4 * half][0], pos, t,
                       1 + half);
-        if (c == nch - 1) {  // this chunk holds position pos: append the step's K/V
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * u, r = i >> 5, c4 = i & 31;
+            if (k0 + r == pos) continue;  // the appended row is staged below
+            *reinterpret_cast<float4*>(sm.Ks + r * kKLd + 4 * c4) = kr[u];
+            *reinterpret_cast<float4*>(sm.Vs + r * kHeadDim + 4 * c4) = vr[u];
+        }
+        if (c == nch - 1) {  // this chunk holds position pos: append the step's K/V (cache and staged row)
+            const int r = pos - k0;
             if (half == 0) {
                 norm_rope_128(qkv + kQDim + j * kHeadDim, knw, sm.kn, &sm.red[0][1], pos, t, 1);
                 kc[(size_t)pos * kKvDim + j * kHeadDim + t] = sm.kn[t];
+                sm.Ks[r * kKLd + t] = sm.kn[t];
             } else {
-                vc[(size_t)pos * kKvDim + j * kHeadDim + t] = qkv[kQDim + kKvDim + j * kHeadDim + t];
+                const float v = qkv[kQDim + kKvDim + j * kHeadDim + t];
+                vc[(size_t)pos * kKvDim + j * kHeadDim + t] = v;
+                sm.Vs[r * kHeadDim + t] = v;
             }
-        }
-        __syncthreads();  // the appended row is visible to the CTA
-        for (int i = tid; i < 64 * 32; i += 256) {
-            const int r = i >> 5, c4 = i & 31;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (r < n) {
-                const size_t o = (size_t)(k0 + r) * kKvDim + j * kHeadDim + 4 * c4;
-                kv = __ldcg(reinterpret_cast<const float4*>(kc + o));
-                vv = __ldcg(reinterpret_cast<const float4*>(vc + o));
-            }
-            *reinterpret_cast<float4*>(sm.Ks + r * kKLd + 4 * c4) = kv;
-            *reinterpret_cast<float4*>(sm.Vs + r * kHeadDim + 4 * c4) = vv;
         }
         __syncthreads();
         // scores: thread (head = half, key = t >> 1, dims (t & 1) * 64 ..)
@@ -388,14 +400,20 @@ __global__ void __launch_bounds__(256) k_attn_step(float* __restrict__ qkv, cons
             if (sm.last) cnt[j] = 0;
         }
         __syncthreads();
-        if (sm.last) {
+        if (sm.last) {  // one pass: the chunks' (max, sum) through shared memory, then the outputs
             const float* ph = part + (size_t)(2 * j + half) * kMaxChunks * kPartStride;
+            float* ml = sm.Ks + half * 2 * kMaxChunks;  // the staged keys are consumed
+            for (int cc = t; cc < nch; cc += 128) {
+                ml[cc] = __ldcg(ph + cc * kPartStride);
+                ml[kMaxChunks + cc] = __ldcg(ph + cc * kPartStride + 1);
+            }
+            __syncthreads();
             float M = -INFINITY;
-            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(ph + cc * kPartStride));
+            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ml[cc]);
             float L = 0.f, acco = 0.f;
             for (int cc = 0; cc < nch; ++cc) {
-                const float w = expf(__ldcg(ph + cc * kPartStride) - M);
-                L = fmaf(__ldcg(ph + cc * kPartStride + 1), w, L);
+                const float w = expf(ml[cc] - M);
+                L = fmaf(ml[kMaxChunks + cc], w, L);
                 acco = fmaf(__ldcg(ph + cc * kPartStride + 2 + t), w, acco);
             }
             out[(2 * j + half) * kHeadDim + t] = acco / L;
