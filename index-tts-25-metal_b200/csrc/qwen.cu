@@ -382,8 +382,13 @@ __global__ void __launch_bounds__(256) k_attn_step(float* __restrict__ qkv, cons
         if (lane == 0) sm.red[warp][1] = ls;
         __syncthreads();
         const float l = sm.red[4 * half][1] + sm.red[4 * half + 1][1] + sm.red[4 * half + 2][1] + sm.red[4 * half + 3][1];
-        float o = 0.f;
-        for (int k = 0; k < n; ++k) o = fmaf(sm.ps[half * 64 + k], sm.Vs[k * kHeadDim + t], o);
+        // four chains over keys k, k+1, k+2, k+3 (rows past n hold p = 0 and zero V)
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int k = 0; k < 64; k += 4)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) o4[u] = fmaf(sm.ps[half * 64 + k + u], sm.Vs[(k + u) * kHeadDim + t], o4[u]);
+        const float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
         float* pp = part + ((size_t)(2 * j + half) * kMaxChunks + c) * kPartStride;
         pp[2 + t] = o;
         if (t == 0) {
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(256) k_attn_step(float* __restrict__ qkv, cons
             pp[1] = l;
         }
         // arrival per KV head; the last of its nch items merges heads 2j, 2j + 1
-        __threadfence();
+        // (the acq_rel add releases the partials the barrier ordered before it)
         __syncthreads();
         if (tid == 0) {
             int prev;
