@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "model.hpp"
 
 namespace itts {
@@ -153,6 +155,32 @@ __device__ __forceinline__ float gelu_ref(float v) {
     if (v > 10.0f) return v;
     if (v < -10.0f) return 0.0f;
     return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
+
+// Programmatic dependent launch (PDL).  A kernel launched with programmatic
+// stream serialization may start while its predecessor in the stream drains:
+// it does what does not depend on it (setup, weight loads), waits for it with
+// pdl_wait() before touching the buffers they share, and calls pdl_trigger()
+// to let its own successor launch early.  Both are no-ops in a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialization (a programmatic edge when the
+// stream is being captured into a graph).
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, int block, size_t smem, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
 
 }  // namespace itts

@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem_base;
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer: the CTA's units in order, one ring stage each
@@ -275,19 +276,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mw_lo)) : "memory");
             int issued = 0;
             const int n = int(u1 - u0);
+            // The first stages' weight tiles do not depend on the previous
+            // kernel (PDL launch): they are requested before the wait for it,
+            // the activation tiles after.  The loop below breaks only at
+            // i >= kStages, so every stage armed here gets its A tiles too.
+            const int early = min(n, kStages);
+            for (int i = 0; i < early; ++i) {
+                const long long u = u0 + i;
+                const int t = int(u / g.kbt), kx = int(u % g.kbt) * GK, n0 = (t % g.ntn) * GN;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&sm.full[i])),
+                             "r"(kStageBytes)
+                             : "memory");
+                tma_load(sm.w[i][0], &mw_hi, kx, n0, &sm.full[i]);
+                tma_load(sm.w[i][1], &mw_lo, kx, n0, &sm.full[i]);
+            }
+            pdl_wait();
             for (int i = 0; i < n; ++i) {
                 const int s = i % kStages;
                 if (i >= kStages && !mbar_wait(&sm.empty[s], uint32_t((i / kStages) + 1) & 1u, &sm.abort)) break;
                 const long long u = u0 + i;
                 const int t = int(u / g.kbt), kx = int(u % g.kbt) * GK;
                 const int m0 = (t / g.ntn) * GM, n0 = (t % g.ntn) * GN;
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&sm.full[s])),
-                             "r"(kStageBytes)
-                             : "memory");
+                if (i >= early) {
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&sm.full[s])),
+                                 "r"(kStageBytes)
+                                 : "memory");
+                    tma_load(sm.w[s][0], &mw_hi, kx, n0, &sm.full[s]);
+                    tma_load(sm.w[s][1], &mw_lo, kx, n0, &sm.full[s]);
+                }
                 tma_load(sm.a[s][0], &ma_hi, kx, m0, &sm.full[s]);
                 tma_load(sm.a[s][1], &ma_lo, kx, m0, &sm.full[s]);
-                tma_load(sm.w[s][0], &mw_hi, kx, n0, &sm.full[s]);
-                tma_load(sm.w[s][1], &mw_lo, kx, n0, &sm.full[s]);
                 issued = i + 1;
             }
             // Loads still in flight land before the CTA may exit (after an abort
@@ -333,6 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_wait(&sm.done, 0u, nullptr);
         }
     } else {  // warps 2-9: drain, then per segment the epilogue
+        pdl_wait();  // the epilogue reads R and writes C, the previous kernel's buffers
         const int q = warp & 3, hcol = (warp - 2) >> 2, dw = warp - 2;
         const int c0 = kDrainCols * hcol;  // this warp's first accumulator column
         const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + uint32_t(c0);
@@ -559,8 +578,8 @@ cudaError_t launch_epi(const CUtensorMap* ma, const CUtensorMap* mw, const GemmA
             cudaFuncSetAttribute(k_gemm_tma<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
     });
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
-    k_gemm_tma<EPI><<<g.ctas, kGemmThreads, kGemmSmemBytes, s>>>(ma[0], ma[1], mw[0], mw[1], g);
-    return cudaGetLastError();
+    return launch_pdl(k_gemm_tma<EPI>, dim3(g.ctas), kGemmThreads, kGemmSmemBytes, s, ma[0], ma[1], mw[0], mw[1],
+                      g);
 }
 
 int sm_count() {

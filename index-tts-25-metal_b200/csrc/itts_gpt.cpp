@@ -86,6 +86,8 @@ struct itts_gpt_ctx {
     const float *spk_w = nullptr, *spk_b = nullptr, *text_emb = nullptr, *text_pos = nullptr, *lang_emb = nullptr;
     float* d_kv = nullptr;
     float *d_hidden = nullptr, *d_x = nullptr, *d_qkv = nullptr, *d_att = nullptr, *d_r = nullptr, *d_ff = nullptr;
+    float* d_att_part = nullptr;  // prefill attention chunk partials (inside the d_hidden block)
+    int* d_att_cnt = nullptr;     // their arrival counters (inside the d_hidden block)
     float* d_act = nullptr;
     itts::DecodeBuffers db{};
     uint32_t* d_history = nullptr;  // {1, 8192}
@@ -308,13 +310,17 @@ void alloc_buffers(itts_gpt_ctx* c) {
     const size_t kv_floats = size_t(c->layers) * 2 * kH * kCap * kHd;
     c->d_kv = dev_alloc<float>(kv_floats, "KV cache allocation");
     const size_t T = 1024;
-    const size_t pre = T * kW * 4 + T * 3840 + T * 5120;  // hidden, x, att, r + qkv + ff
+    // hidden, x, att, r + qkv + ff + attention partials + their counters
+    const size_t pre = T * kW * 4 + T * 3840 + T * 5120 + itts::kAttPartFloats + itts::kAttCounters;
     c->d_hidden = dev_alloc<float>(pre, "prefill scratch");
     c->d_x = c->d_hidden + T * kW;
     c->d_att = c->d_x + T * kW;
     c->d_r = c->d_att + T * kW;
     c->d_qkv = c->d_r + T * kW;
     c->d_ff = c->d_qkv + T * 3840;
+    c->d_att_part = c->d_ff + T * 5120;
+    c->d_att_cnt = reinterpret_cast<int*>(c->d_att_part + itts::kAttPartFloats);
+    ck(cudaMemset(c->d_att_cnt, 0, itts::kAttCounters * sizeof(int)), "prefill scratch");
     // decode activations (each region 256-byte aligned): the tagged hand-off
     // words (qkv, h, hm, attn, f), logits, attention partials, control block
     const size_t sizes[8] = {3840 * 8, kW * 8, kW * 8, kW * 8, 5120 * 8, 8448 * 4, size_t(kH) * 256 * 68 * 4,
@@ -421,7 +427,7 @@ itts::TmaPrefill* tma_of(itts_gpt_ctx* c) { return c->prefill_mode == 0 && c->tm
 void run_prefill(itts_gpt_ctx* c, uint32_t rows) {
     itts::PrefillArgs p{&c->hw,   c->d_hidden, c->d_x,    c->d_qkv,  c->d_att,
                         c->d_r,   c->d_ff,     c->d_kv,   int(rows), c->dtype == ITTS_WEIGHTS_BF16,
-                        c->db.ctl->status,     tma_of(c)};
+                        c->db.ctl->status,     tma_of(c), c->d_att_part, c->d_att_cnt};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     reset_ctl(c);
     itts::DecodeArgs a = decode_args(c);
@@ -605,7 +611,9 @@ void batch_prefill(itts_gpt_ctx* c, const float* prefix, size_t n_floats, uint32
                         int(rows),
                         c->dtype == ITTS_WEIGHTS_BF16,
                         c->db.ctl->status,
-                        tma_of(c)};
+                        tma_of(c),
+                        c->d_att_part,
+                        c->d_att_cnt};
     ck(itts::launch_prefill_layers(p, c->stream, &c->launches), "prefill launch");
     itts::DecodeArgs a = decode_args(c);
     a.head_src = c->d_hidden + size_t(rows - 1) * kW;

@@ -252,7 +252,16 @@ struct PrefillArgs {
     bool wbf16;   // matrices stored bf16
     int* status;  // device status word (bounded waits of the tensor-core GEMM)
     TmaPrefill* tma;  // the TMA-fed tensor-core GEMM; null: CUDA-core tiles
+    float* att_part;  // attention key-chunk partials [kHeads][kAttMaxBlocks][kAttMaxChunks][64][kAttPartLd]
+    int* att_cnt;     // chunk arrivals per (head, query block) [kHeads * kAttMaxBlocks], zero between launches
 };
+// Prefill attention split: 64-query blocks, key chunks of kAttChunk keys.
+constexpr int kAttChunk = 128;
+constexpr int kAttMaxBlocks = 16;  // 1024 prefix rows
+constexpr int kAttMaxChunks = kAttMaxBlocks * 64 / kAttChunk;
+constexpr int kAttPartLd = 68;
+constexpr size_t kAttPartFloats = size_t(20) * kAttMaxBlocks * kAttMaxChunks * 64 * kAttPartLd;
+constexpr int kAttCounters = 20 * kAttMaxBlocks;
 cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t* launches);
 
 cudaError_t launch_transpose(const float* in, float* out, int rows_in, int cols_in, cudaStream_t s);

@@ -18,6 +18,8 @@ __global__ void __launch_bounds__(256) k_ln_rows(const float* __restrict__ x, co
                                                  const float* __restrict__ b, float* __restrict__ out,
                                                  float* __restrict__ out_lo) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();  // x is the previous kernel's output
     const float* row = x + (size_t)blockIdx.x * kWidth;
     float v[5];
     float s = 0.f;
@@ -150,6 +152,8 @@ __global__ void __launch_bounds__(256) k_gemm_nt(const float* __restrict__ A, co
 // mit2_gpt_kv_store_f32 (kernels.metal:1250-1266) into the head-major cache
 // [K|V][head][4096][64] of one layer.
 __global__ void k_kv_store(const float* __restrict__ qkv, float* __restrict__ kv_layer, int T) {
+    pdl_trigger();
+    pdl_wait();
     const size_t n = (size_t)T * 2 * kWidth;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / (2 * kWidth)), rem = (int)(i % (2 * kWidth));
@@ -161,15 +165,23 @@ __global__ void k_kv_store(const float* __restrict__ qkv, float* __restrict__ kv
 // Causal multi-head attention over packed qkv [T, 3840] (q | k | v, head h at
 // h*64), scale 1/8, as mit2_gpt_causal_attention_sgq_f32
 // (kernels.metal:2249-2290), with an online softmax over 64-key tiles.
-// CTA = (head, 64 queries), 256 threads as 16 x 16: thread (ty, tx) owns the
-// scores of queries 4ty..4ty+3 x keys 4tx..4tx+3 of a tile and the outputs of
-// those queries x dims 4tx..4tx+3.  Q and K are staged d-major (QT[d][q],
-// KT[d][k]) and V and the tile's probabilities row-major, so every inner step
-// is two or eight 16-byte shared loads per 16 or 64 FMAs.  A query row's 64
-// scores live in one half-warp, reduced with shuffles.
+// CTA = (head, 64 queries, chunk of kAttChunk keys): the keys a query block
+// reaches are split into chunks so that no CTA walks more than two tiles (a
+// single CTA per block left the last blocks of long prefixes as the critical
+// path).  256 threads as 16 x 16: thread (ty, tx) owns the scores of queries
+// 4ty..4ty+3 x keys 4tx..4tx+3 of a tile and the outputs of those queries x
+// dims 4tx..4tx+3.  Q and K are staged d-major (QT[d][q], KT[d][k]) and V and
+// the tile's probabilities row-major, so every inner step is two or eight
+// 16-byte shared loads per 16 or 64 FMAs.  A query row's 64 scores live in one
+// half-warp, reduced with shuffles.
+// A block with one chunk writes its output; otherwise every chunk writes its
+// (max, sum, unnormalised output) partial and the last of the block's chunks to
+// arrive merges them in chunk order (deterministic whichever arrives last).
 // With `out_lo` the output is written split (as k_ln_rows).
 constexpr int kAttLd = 68;  // row stride of the staged 64 x 64 tiles (floats)
 constexpr size_t kAttSmem = 4 * 64 * kAttLd * sizeof(float);
+static_assert(kAttChunk % 64 == 0, "key chunks are whole tiles");
+static_assert(kAttPartLd >= 66 && kAttPartLd % 4 == 0, "partial rows: 64 outputs, max, sum");
 
 __device__ __forceinline__ float half_max(float v) {
 #pragma unroll
@@ -182,16 +194,34 @@ __device__ __forceinline__ float half_sum(float v) {
     return v;
 }
 
+__device__ __forceinline__ void attn_store(float* out, float* out_lo, size_t o, float4 y) {
+    if (out_lo) {
+        const float4 hv = make_float4(rn_tf32(y.x), rn_tf32(y.y), rn_tf32(y.z), rn_tf32(y.w));
+        *reinterpret_cast<float4*>(out + o) = hv;
+        *reinterpret_cast<float4*>(out_lo + o) =
+            make_float4(rn_tf32(y.x - hv.x), rn_tf32(y.y - hv.y), rn_tf32(y.z - hv.z), rn_tf32(y.w - hv.w));
+    } else {
+        *reinterpret_cast<float4*>(out + o) = y;
+    }
+}
+
 __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ qkv, float* __restrict__ out,
-                                                     float* __restrict__ out_lo, int T) {
+                                                     float* __restrict__ out_lo, int T, float* part, int* cnt) {
     extern __shared__ __align__(16) float att_smem[];
+    __shared__ int is_last;
     float* QT = att_smem;             // [64 d][kAttLd]: Q of the block, d-major
     float* KT = QT + 64 * kAttLd;     // [64 d][kAttLd]: K of the tile, d-major
     float* Vs = KT + 64 * kAttLd;     // [64 k][kAttLd]
     float* Ps = Vs + 64 * kAttLd;     // [64 q][kAttLd]: the tile's probabilities
-    const int h = blockIdx.x, q0 = blockIdx.y * 64, tid = threadIdx.x;
+    const int h = blockIdx.x, qb = blockIdx.y, q0 = qb * 64, tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const int lr = tid & 63, ld4 = tid >> 6;  // staging: row lr, 16-byte column groups ld4, ld4 + 4, ...
+    const int kend = min(T, q0 + 64);  // keys 0 .. kend-1 reach some query of the block
+    const int nck = (kend + kAttChunk - 1) / kAttChunk;
+    pdl_trigger();
+    if ((int)blockIdx.z >= nck) return;  // the grid covers the longest block's chunks
+    const int kb = blockIdx.z * kAttChunk, ke = min(kend, kb + kAttChunk);
+    pdl_wait();
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int d = 4 * (ld4 + 4 * j), q = q0 + lr;
@@ -210,14 +240,13 @@ __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ q
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
     }
-    const int kend = min(T, q0 + 64);  // keys 0 .. kend-1 reach some query of the block
-    for (int k0 = 0; k0 < kend; k0 += 64) {
+    for (int k0 = kb; k0 < ke; k0 += 64) {
         __syncthreads();  // the previous tile's K, V and P are consumed
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int d = 4 * (ld4 + 4 * j), key = k0 + lr;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (key < kend) {
+            if (key < ke) {
                 const float* row = qkv + (size_t)key * kQkv + h * kHeadDim + d;
                 kv = *reinterpret_cast<const float4*>(row + kWidth);
                 vv = *reinterpret_cast<const float4*>(row + 2 * kWidth);
@@ -251,7 +280,7 @@ __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ q
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
                 const int key = k0 + 4 * tx + b;
-                sc[a][b] = (key <= q && key < kend) ? sc[a][b] * 0.125f : -INFINITY;
+                sc[a][b] = (key <= q && key < ke) ? sc[a][b] * 0.125f : -INFINITY;
                 mx = fmaxf(mx, sc[a][b]);
             }
             const float mn = fmaxf(m[a], half_max(mx));
@@ -291,25 +320,67 @@ __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ q
             }
         }
     }
+    if (nck == 1) {
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int q = q0 + 4 * ty + a;
+            if (q >= T) continue;
+            const float inv = 1.0f / l[a];
+            attn_store(out, out_lo, (size_t)q * kWidth + h * kHeadDim + 4 * tx,
+                       make_float4(acc[a][0] * inv, acc[a][1] * inv, acc[a][2] * inv, acc[a][3] * inv));
+        }
+        return;
+    }
+    // partial of chunk z: row r = [64 outputs | max | sum | pad]
+    float* blk = part + ((size_t)h * kAttMaxBlocks + qb) * kAttMaxChunks * 64 * kAttPartLd;
+    float* mine = blk + (size_t)blockIdx.z * 64 * kAttPartLd;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
-        const int q = q0 + 4 * ty + a;
-        if (q >= T) continue;
-        const float inv = 1.0f / l[a];
-        const float4 y = make_float4(acc[a][0] * inv, acc[a][1] * inv, acc[a][2] * inv, acc[a][3] * inv);
-        const size_t o = (size_t)q * kWidth + h * kHeadDim + 4 * tx;
-        if (out_lo) {
-            const float4 hv = make_float4(rn_tf32(y.x), rn_tf32(y.y), rn_tf32(y.z), rn_tf32(y.w));
-            *reinterpret_cast<float4*>(out + o) = hv;
-            *reinterpret_cast<float4*>(out_lo + o) =
-                make_float4(rn_tf32(y.x - hv.x), rn_tf32(y.y - hv.y), rn_tf32(y.z - hv.z), rn_tf32(y.w - hv.w));
-        } else {
-            *reinterpret_cast<float4*>(out + o) = y;
+        float* row = mine + (4 * ty + a) * kAttPartLd;
+        *reinterpret_cast<float4*>(row + 4 * tx) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+        if (tx == 0) *reinterpret_cast<float2*>(row + 64) = make_float2(m[a], l[a]);
+    }
+    __syncthreads();  // every partial store of this CTA is issued
+    if (tid == 0) {
+        // The acq_rel add releases the stores the barrier ordered before it
+        // and, for the last arriver, acquires the other chunks'.
+        int* c = cnt + h * kAttMaxBlocks + qb;
+        int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(c) : "memory");
+        const int last = prev == nck - 1;
+        if (last) *c = 0;
+        is_last = last;
+    }
+    __syncthreads();
+    if (!is_last) return;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int r = 4 * ty + a, q = q0 + r;
+        if (q >= T) continue;  // (no key reaches a padding row: its max is -inf)
+        float mx = -INFINITY;
+        for (int c = 0; c < nck; ++c) mx = fmaxf(mx, __ldcg(blk + ((size_t)c * 64 + r) * kAttPartLd + 64));
+        float sum = 0.f;
+        float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < nck; ++c) {  // chunk order
+            const float* row = blk + ((size_t)c * 64 + r) * kAttPartLd;
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(row + 64));
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + 4 * tx));
+            const float w = expf(ml.x - mx);  // every chunk holds key 0 or a key <= the block's first query
+            sum = fmaf(ml.y, w, sum);
+            y.x = fmaf(v.x, w, y.x);
+            y.y = fmaf(v.y, w, y.y);
+            y.z = fmaf(v.z, w, y.z);
+            y.w = fmaf(v.w, w, y.w);
         }
+        const float inv = 1.0f / sum;
+        attn_store(out, out_lo, (size_t)q * kWidth + h * kHeadDim + 4 * tx,
+                   make_float4(y.x * inv, y.y * inv, y.z * inv, y.w * inv));
     }
 }
 
-static cudaError_t launch_attn(const float* qkv, float* out, float* out_lo, int T, cudaStream_t s) {
+static cudaError_t launch_attn(const PrefillArgs& p, float* out, float* out_lo, cudaStream_t s) {
+    const int T = p.T;
+    if (T < 1 || T > kAttMaxBlocks * 64) return cudaErrorInvalidValue;
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -320,8 +391,9 @@ static cudaError_t launch_attn(const float* qkv, float* out, float* out_lo, int 
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    k_causal_attn<<<dim3(kHeads, (T + 63) / 64), 256, kAttSmem, s>>>(qkv, out, out_lo, T);
-    return cudaGetLastError();
+    const dim3 grid(kHeads, (T + 63) / 64, (T + kAttChunk - 1) / kAttChunk);
+    return launch_pdl(k_causal_attn, grid, 256, kAttSmem, s, (const float*)p.qkv, out, out_lo, T, p.att_part,
+                      p.att_cnt);
 }
 
 cudaError_t launch_gemm_tma(TmaPrefill* p, int layer, int mat, const float* bias, const float* R, float* C,
@@ -341,23 +413,32 @@ static void gemm(const float* A, const float* W, bool wb, const float* bias, con
 
 // Prefill mode 0: the TMA-fed tensor-core GEMM (gemm_tma.cu); the operands of
 // every GEMM are split into TF32 hi / lo by the kernel that produces them.
+// Every kernel of the chain is launched with PDL: it starts while its
+// predecessor drains (the GEMM requests its first weight tiles then) and
+// waits for it before touching shared buffers, so a kernel completes only
+// after all before it have.
 static cudaError_t prefill_layers_tma(const PrefillArgs& p, cudaStream_t s, uint64_t* launches) {
     const int T = p.T;
     TmaPrefill* q = p.tma;
     // A CTA that gave up leaves its tile's split-K counter behind.
     cudaError_t e = cudaMemsetAsync(q->counters, 0, TmaPrefill::kCounters * sizeof(int), s);
     if (e != cudaSuccess) return e;
+    const int kv_grid = min(1184, (T * 2 * kWidth + 255) / 256);
     for (int l = 0; l < p.hw->layers; ++l) {
         const LayerW& L = p.hw->layer[l];
-        k_ln_rows<<<T, 256, 0, s>>>(p.hidden, L.ln1_g, L.ln1_b, q->x_hi, q->x_lo);
+        if ((e = launch_pdl(k_ln_rows, dim3(T), 256, 0, s, p.hidden, L.ln1_g, L.ln1_b, q->x_hi, q->x_lo)) !=
+            cudaSuccess)
+            return e;
         if ((e = launch_gemm_tma(q, l, kMatQkv, L.b_qkv, nullptr, p.qkv, nullptr, T, p.status, s)) != cudaSuccess)
             return e;
-        k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
-            p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
-        if ((e = launch_attn(p.qkv, q->att_hi, q->att_lo, T, s)) != cudaSuccess) return e;
+        if ((e = launch_pdl(k_kv_store, dim3(kv_grid), 256, 0, s, p.qkv,
+                            p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T)) != cudaSuccess)
+            return e;
+        if ((e = launch_attn(p, q->att_hi, q->att_lo, s)) != cudaSuccess) return e;
         if ((e = launch_gemm_tma(q, l, kMatO, L.b_o, p.hidden, p.r, nullptr, T, p.status, s)) != cudaSuccess)
             return e;
-        k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, q->x_hi, q->x_lo);
+        if ((e = launch_pdl(k_ln_rows, dim3(T), 256, 0, s, p.r, L.ln2_g, L.ln2_b, q->x_hi, q->x_lo)) != cudaSuccess)
+            return e;
         if ((e = launch_gemm_tma(q, l, kMatFc, L.b_fc, nullptr, q->ff_hi, q->ff_lo, T, p.status, s)) != cudaSuccess)
             return e;
         if ((e = launch_gemm_tma(q, l, kMatMp, L.b_mp, p.r, p.hidden, nullptr, T, p.status, s)) != cudaSuccess)
@@ -376,7 +457,7 @@ cudaError_t launch_prefill_layers(const PrefillArgs& p, cudaStream_t s, uint64_t
         gemm<kEpiBias>(p.x, L.w_qkv, p.wbf16, L.b_qkv, nullptr, p.qkv, T, kQkv, kWidth, s);
         k_kv_store<<<min(1184, (T * 2 * kWidth + 255) / 256), 256, 0, s>>>(
             p.qkv, p.kv + (size_t)l * 2 * kHeads * kKvCapacity * kHeadDim, T);
-        if (cudaError_t e = launch_attn(p.qkv, p.att, nullptr, T, s); e != cudaSuccess) return e;
+        if (cudaError_t e = launch_attn(p, p.att, nullptr, s); e != cudaSuccess) return e;
         gemm<kEpiResid>(p.att, L.w_o, p.wbf16, L.b_o, p.hidden, p.r, T, kWidth, kWidth, s);
         k_ln_rows<<<T, 256, 0, s>>>(p.r, L.ln2_g, L.ln2_b, p.x, nullptr);
         gemm<kEpiGelu>(p.x, L.w_fc, p.wbf16, L.b_fc, nullptr, p.ff, T, kFfn, kWidth, s);

@@ -268,8 +268,6 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* __restrict__ 
 // The decode kernels are launched with programmatic stream serialization
 // (PDL): each may start while its predecessor drains, does what does not
 // depend on it (the GEMVs load their weight rows), then waits for it.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Decode attention of one step, with the q/k RMSNorm + RoPE of the step's
 // token and its K/V append folded in.  A fixed grid of CTAs walks the work
@@ -569,23 +567,6 @@ __global__ void k_interleave_rows(const float* __restrict__ a, const float* __re
         const size_t r = i / cols, c = i % cols;
         out[i] = (r & 1) ? b[(r >> 1) * cols + c] : a[(r >> 1) * cols + c];
     }
-}
-
-// Launch with programmatic stream serialization (captured as a programmatic
-// edge inside the decode-step graph).
-template <class... P, class... A>
-cudaError_t launch_pdl(void (*kernel)(P...), int grid, int block, size_t smem, cudaStream_t s, A&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
 
 template <int K, int EPI, bool NORM>
