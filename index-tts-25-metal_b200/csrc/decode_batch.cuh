@@ -73,6 +73,7 @@ struct BGeo {
 struct BUnits {
     uint32_t start[kMaxBatch + 1];  // first unit of each row
     uint32_t nch[kMaxBatch], ch[kMaxBatch], S[kMaxBatch];
+    uint32_t arena[kMaxBatch];      // KV arena of each row
 };
 
 // Attention scratch for P units at a time: the 16 virtual-warp states of
@@ -430,26 +431,127 @@ __device__ bool bgemv_long(BCtx& cx, int nrows, uint32_t act, int where, Epi epi
 }
 
 // --------------------------------------------------------------- attention
-__device__ __forceinline__ void batch_units(const BatchArgs& a, int ncta, uint32_t act, uint32_t gstep, BUnits& u) {
-    uint32_t acc = 0;
-    for (uint32_t m = 0; m < a.M; ++m) {
-        u.start[m] = acc;
-        u.nch[m] = u.ch[m] = u.S[m] = 0;
-        if (!((act >> m) & 1u)) continue;
-        const uint32_t S = a.st->s0[m] + row_fwd(a, m, gstep), keys = S + 1;
-        const uint32_t ch = attn_chunk(keys, ncta);
-        u.S[m] = S;
-        u.ch[m] = ch;
-        u.nch[m] = (keys + ch - 1) / ch;
-        acc += kHeads * u.nch[m];
-    }
-    u.start[a.M] = acc;
-}
-
-__device__ __forceinline__ float* arena_kv(const BatchArgs& a, uint32_t m, int li, int kv, uint32_t h) {
-    return a.kv + (size_t)a.st->arena[m] * a.arena_floats +
+__device__ __forceinline__ float* arena_kv(const BatchArgs& a, const BUnits& u, uint32_t m, int li, int kv,
+                                           uint32_t h) {
+    return a.kv + (size_t)u.arena[m] * a.arena_floats +
            (((size_t)li * 2 + kv) * kHeads + h) * (size_t)kKvCapacity * kHeadDim;
 }
+
+// Called by warp 0: lane m reads row m's state (one round trip for all rows),
+// then lane 0 accumulates the unit offsets.
+__device__ __forceinline__ void batch_units(const BatchArgs& a, int ncta, uint32_t act, uint32_t gstep, BUnits& u) {
+    const uint32_t m = threadIdx.x;
+    if (m < a.M) {
+        u.nch[m] = u.ch[m] = u.S[m] = 0;
+        u.arena[m] = a.st->arena[m];
+        if ((act >> m) & 1u) {
+            const uint32_t S = a.st->s0[m] + row_fwd(a, m, gstep), keys = S + 1;
+            const uint32_t ch = attn_chunk(keys, ncta);
+            u.S[m] = S;
+            u.ch[m] = ch;
+            u.nch[m] = (keys + ch - 1) / ch;
+        }
+    }
+    __syncwarp();
+    if (m == 0) {
+        uint32_t acc = 0;
+        for (uint32_t r = 0; r < a.M; ++r) {
+            u.start[r] = acc;
+            acc += kHeads * u.nch[r];
+        }
+        u.start[a.M] = acc;
+    }
+}
+
+// Virtual warp `warp` of R units of a pass at once, when every unit's chunk
+// has at most 128 / R keys (so each virtual warp meets at most 8 / R keys of a
+// unit, one batch-1 block): the K/V loads of the R units share one round
+// trip, kept in the same eight load registers, unit r in slots
+// [r * 8 / R, (r + 1) * 8 / R).  Each unit's block is then computed exactly as
+// the batch-1 loop computes it: its keys in its slots, the block's other
+// slots (keys past the chunk) as zero vectors with -inf scores.
+template <int R, int P>
+__device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAttnSmem<P>& sm, int i0, int np,
+                                                int warp, int lane) {
+    constexpr int kKB = 8, W = kKB / R;
+    float2 kv[kKB], vv[kKB];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = i0 + r;
+        uint32_t m = 0, h = 0, S = 0, k0 = 0, k1 = 0;
+        if (i < np) {
+            m = sm.um[i];
+            h = sm.uh[i];
+            const uint32_t ch = sm.units.ch[m];
+            S = sm.units.S[m];
+            k0 = sm.uc[i] * ch;
+            k1 = min(k0 + ch, S + 1);
+        }
+        const float* Kc = arena_kv(a, sm.units, m, li, 0, h);
+        const float* Vc = arena_kv(a, sm.units, m, li, 1, h);
+#pragma unroll
+        for (int ii = 0; ii < W; ++ii) {
+            const uint32_t kk = k0 + warp + ii * kWarps;
+            float2 kx = make_float2(0.f, 0.f), vx = kx;
+            if (i < np && kk < k1) {
+                if (kk < S) {
+                    kx = __ldcg(reinterpret_cast<const float2*>(Kc + (size_t)kk * kHeadDim) + lane);
+                    vx = __ldcg(reinterpret_cast<const float2*>(Vc + (size_t)kk * kHeadDim) + lane);
+                } else {
+                    kx = *reinterpret_cast<const float2*>(sm.qkvh[i] + kHeadDim + 2 * lane);
+                    vx = *reinterpret_cast<const float2*>(sm.qkvh[i] + 2 * kHeadDim + 2 * lane);
+                }
+            }
+            kv[r * W + ii] = kx;
+            vv[r * W + ii] = vx;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = i0 + r;
+        if (i >= np) break;
+        const uint32_t m = sm.um[i], ch = sm.units.ch[m];
+        const uint32_t k0 = sm.uc[i] * ch, k1 = min(k0 + ch, sm.units.S[m] + 1), kb = k0 + warp;
+        float mx = -INFINITY, l = 0.f;
+        float2 o = make_float2(0.f, 0.f);
+        if (kb < k1) {  // the batch-1 loop runs once for this virtual warp
+            const float2 q = *reinterpret_cast<const float2*>(sm.qkvh[i] + 2 * lane);
+            float sk[kKB];
+#pragma unroll
+            for (int ii = 0; ii < W; ++ii) sk[ii] = fmaf(q.x, kv[r * W + ii].x, q.y * kv[r * W + ii].y);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                for (int ii = 0; ii < W; ++ii) sk[ii] += __shfl_xor_sync(0xffffffffu, sk[ii], off);
+            float mn = mx;
+#pragma unroll
+            for (int ii = 0; ii < kKB; ++ii) {
+                sk[ii] = ii < W && kb + ii * kWarps < k1 ? sk[ii] * 0.125f : -INFINITY;
+                mn = fmaxf(mn, sk[ii]);
+            }
+            const float corr = expf(mx - mn);
+            l *= corr;
+            o.x *= corr;
+            o.y *= corr;
+#pragma unroll
+            for (int ii = 0; ii < kKB; ++ii) {
+                const float p = expf(sk[ii] - mn);
+                const float2 v = ii < W ? vv[r * W + ii] : make_float2(0.f, 0.f);
+                l += p;
+                o.x = fmaf(p, v.x, o.x);
+                o.y = fmaf(p, v.y, o.y);
+            }
+            mx = mn;
+        }
+        if (lane == 0) {
+            sm.vm[i][warp] = mx;
+            sm.vl[i][warp] = l;
+        }
+        sm.vo[i][warp][2 * lane] = o.x;
+        sm.vo[i][warp][2 * lane + 1] = o.y;
+    }
+}
+
 
 // Split-K attention of layer li for every active row, P units of this CTA at
 // a time (kernels.metal:2064-2145; batch-1 phase_attn per unit).  Called by
@@ -458,7 +560,7 @@ template <int P>
 __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t gstep, int cta, int ncta,
                             BAttnSmem<P>& sm) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    if (t == 0) batch_units(a, ncta, act, gstep, sm.units);
+    if (warp == 0) batch_units(a, ncta, act, gstep, sm.units);
     csync();
     const uint32_t total = sm.units.start[a.M];
 #pragma unroll 1
@@ -488,13 +590,22 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
         }
         csync();
         // virtual warp `warp` of every unit: the batch-1 per-warp online softmax
+        uint32_t chmax = 0;
+        for (int i = 0; i < np; ++i) chmax = max(chmax, sm.units.ch[sm.um[i]]);
+        if (chmax <= 32) {
+#pragma unroll 1
+            for (int i0 = 0; i0 < np; i0 += 4) battn_vw_packed<4>(a, li, sm, i0, np, warp, lane);
+        } else if (chmax <= 64) {
+#pragma unroll 1
+            for (int i0 = 0; i0 < np; i0 += 2) battn_vw_packed<2>(a, li, sm, i0, np, warp, lane);
+        } else {
 #pragma unroll 1
         for (int i = 0; i < np; ++i) {
             const uint32_t m = sm.um[i], h = sm.uh[i], c = sm.uc[i];
             const uint32_t S = sm.units.S[m], ch = sm.units.ch[m], keys = S + 1;
             const uint32_t k0 = c * ch, k1 = min(k0 + ch, keys);
-            const float* Kc = arena_kv(a, m, li, 0, h);
-            const float* Vc = arena_kv(a, m, li, 1, h);
+            const float* Kc = arena_kv(a, sm.units, m, li, 0, h);
+            const float* Vc = arena_kv(a, sm.units, m, li, 1, h);
             const float* kcur = sm.qkvh[i] + kHeadDim;
             const float* vcur = sm.qkvh[i] + 2 * kHeadDim;
             const float2 q = *reinterpret_cast<const float2*>(sm.qkvh[i] + 2 * lane);
@@ -551,6 +662,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
             sm.vo[i][warp][2 * lane] = o.x;
             sm.vo[i][warp][2 * lane + 1] = o.y;
         }
+        }
         csync();
         // merge the 16 states of each unit (warp order), write its partial, append K/V
         if (t < np * kHeadDim) {
@@ -577,7 +689,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
             const int i = tt / (2 * kHeadDim), r = tt % (2 * kHeadDim);
             const uint32_t m = sm.um[i];
             if (sm.uc[i] == sm.units.nch[m] - 1) {
-                float* dst = arena_kv(a, m, li, r / kHeadDim, sm.uh[i]) + (size_t)sm.units.S[m] * kHeadDim;
+                float* dst = arena_kv(a, sm.units, m, li, r / kHeadDim, sm.uh[i]) + (size_t)sm.units.S[m] * kHeadDim;
                 dst[r % kHeadDim] = sm.qkvh[i][kHeadDim + r];
             }
         }
@@ -630,7 +742,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
 // attention phase reads them from L2.
 __device__ void bprefetch_kv(const BatchArgs& a, int cta, int ncta, int li, uint32_t act, uint32_t gstep,
                              BUnits& u) {
-    if (threadIdx.x == 0) batch_units(a, ncta, act, gstep, u);
+    if (threadIdx.x < 32) batch_units(a, ncta, act, gstep, u);
     csync();
     const uint32_t total = u.start[a.M];
     for (uint32_t x = cta; x < total; x += ncta) {
@@ -642,7 +754,7 @@ __device__ void bprefetch_kv(const BatchArgs& a, int cta, int ncta, int li, uint
         const uint32_t lines = 4 * (k1 - k0);  // K and V, two lines per 64-float row
         for (uint32_t l = threadIdx.x; l < lines; l += kThreads) {
             const uint32_t kv = l / (2 * (k1 - k0)), rem = l % (2 * (k1 - k0));
-            const float* p = arena_kv(a, m, li, (int)kv, h) + (size_t)(k0 + (rem >> 1)) * kHeadDim + (rem & 1) * 32;
+            const float* p = arena_kv(a, u, m, li, (int)kv, h) + (size_t)(k0 + (rem >> 1)) * kHeadDim + (rem & 1) * 32;
             asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
         }
     }
