@@ -83,7 +83,7 @@ struct BAttnSmem {
     float vm[P][kWarps], vl[P][kWarps];
     float vo[P][kWarps][kHeadDim];
     __align__(16) float qkvh[P][3 * kHeadDim];
-    uint32_t um[P], uh[P], uc[P];
+    uint32_t um[2][P], uh[2][P], uc[2][P];  // (row, head, chunk) of the pass's units; two passes' worth
     int last[P];
     BUnits units;
 };
@@ -471,8 +471,9 @@ __device__ __forceinline__ void batch_units(const BatchArgs& a, int ncta, uint32
 // the batch-1 loop computes it: its keys in its slots, the block's other
 // slots (keys past the chunk) as zero vectors with -inf scores.
 template <int R, int P>
-__device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAttnSmem<P>& sm, int i0, int np,
-                                                int warp, int lane) {
+__device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAttnSmem<P>& sm, const uint32_t* um,
+                                                const uint32_t* uh, const uint32_t* uc, int i0, int np, int warp,
+                                                int lane) {
     constexpr int kKB = 8, W = kKB / R;
     float2 kv[kKB], vv[kKB];
 #pragma unroll
@@ -480,11 +481,11 @@ __device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAtt
         const int i = i0 + r;
         uint32_t m = 0, h = 0, S = 0, k0 = 0, k1 = 0;
         if (i < np) {
-            m = sm.um[i];
-            h = sm.uh[i];
+            m = um[i];
+            h = uh[i];
             const uint32_t ch = sm.units.ch[m];
             S = sm.units.S[m];
-            k0 = sm.uc[i] * ch;
+            k0 = uc[i] * ch;
             k1 = min(k0 + ch, S + 1);
         }
         const float* Kc = arena_kv(a, sm.units, m, li, 0, h);
@@ -510,8 +511,8 @@ __device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAtt
     for (int r = 0; r < R; ++r) {
         const int i = i0 + r;
         if (i >= np) break;
-        const uint32_t m = sm.um[i], ch = sm.units.ch[m];
-        const uint32_t k0 = sm.uc[i] * ch, k1 = min(k0 + ch, sm.units.S[m] + 1), kb = k0 + warp;
+        const uint32_t m = um[i], ch = sm.units.ch[m];
+        const uint32_t k0 = uc[i] * ch, k1 = min(k0 + ch, sm.units.S[m] + 1), kb = k0 + warp;
         float mx = -INFINITY, l = 0.f;
         float2 o = make_float2(0.f, 0.f);
         if (kb < k1) {  // the batch-1 loop runs once for this virtual warp
@@ -560,48 +561,55 @@ template <int P>
 __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t gstep, int cta, int ncta,
                             BAttnSmem<P>& sm) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    if (warp == 0) batch_units(a, ncta, act, gstep, sm.units);
+    // Lane t < P of warp 0 finds unit t of the pass starting at unit `base`.
+    auto assign = [&](uint32_t base, int b) {
+        const uint32_t u = base + (uint32_t)t * ncta, total = sm.units.start[a.M];
+        if (u < total) {
+            uint32_t m = 0;
+            while (u >= sm.units.start[m + 1]) ++m;
+            const uint32_t r = u - sm.units.start[m];
+            sm.um[b][t] = m;
+            sm.uh[b][t] = r / sm.units.nch[m];
+            sm.uc[b][t] = r % sm.units.nch[m];
+        } else {
+            sm.um[b][t] = 0xffffffffu;
+        }
+    };
+    if (warp == 0) {
+        batch_units(a, ncta, act, gstep, sm.units);
+        __syncwarp();
+        if (t < P) assign((uint32_t)cta, 0);
+    }
     csync();
     const uint32_t total = sm.units.start[a.M];
+    int pass = 0;
 #pragma unroll 1
-    for (uint32_t base = cta; base < total; base += (uint32_t)ncta * P) {
-        if (t < P) {
-            const uint32_t u = base + (uint32_t)t * ncta;
-            if (u < total) {
-                uint32_t m = 0;
-                while (u >= sm.units.start[m + 1]) ++m;
-                const uint32_t r = u - sm.units.start[m];
-                sm.um[t] = m;
-                sm.uh[t] = r / sm.units.nch[m];
-                sm.uc[t] = r % sm.units.nch[m];
-            } else {
-                sm.um[t] = 0xffffffffu;
-            }
-        }
-        csync();
+    for (uint32_t base = cta; base < total; base += (uint32_t)ncta * P, ++pass) {
+        const int b = pass & 1;
+        const uint32_t *um = sm.um[b], *uh = sm.uh[b], *uc = sm.uc[b];
         int np = 0;
-        for (int i = 0; i < P; ++i) np += sm.um[i] != 0xffffffffu;
+        for (int i = 0; i < P; ++i) np += um[i] != 0xffffffffu;
         // q, k, v of each unit's head: 3 x 16 threads x 4 floats per unit
         if (t < np * 48) {
             const int i = t / 48, part = (t % 48) >> 4, q4 = t & 15;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.qkv + (size_t)sm.um[i] * kQkv + part * kWidth +
-                                                                    sm.uh[i] * kHeadDim) + q4);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.qkv + (size_t)um[i] * kQkv + part * kWidth +
+                                                                    uh[i] * kHeadDim) + q4);
             *reinterpret_cast<float4*>(&sm.qkvh[i][part * kHeadDim + 4 * q4]) = v;
         }
         csync();
         // virtual warp `warp` of every unit: the batch-1 per-warp online softmax
         uint32_t chmax = 0;
-        for (int i = 0; i < np; ++i) chmax = max(chmax, sm.units.ch[sm.um[i]]);
+        for (int i = 0; i < np; ++i) chmax = max(chmax, sm.units.ch[um[i]]);
         if (chmax <= 32) {
 #pragma unroll 1
-            for (int i0 = 0; i0 < np; i0 += 4) battn_vw_packed<4>(a, li, sm, i0, np, warp, lane);
+            for (int i0 = 0; i0 < np; i0 += 4) battn_vw_packed<4>(a, li, sm, um, uh, uc, i0, np, warp, lane);
         } else if (chmax <= 64) {
 #pragma unroll 1
-            for (int i0 = 0; i0 < np; i0 += 2) battn_vw_packed<2>(a, li, sm, i0, np, warp, lane);
+            for (int i0 = 0; i0 < np; i0 += 2) battn_vw_packed<2>(a, li, sm, um, uh, uc, i0, np, warp, lane);
         } else {
 #pragma unroll 1
         for (int i = 0; i < np; ++i) {
-            const uint32_t m = sm.um[i], h = sm.uh[i], c = sm.uc[i];
+            const uint32_t m = um[i], h = uh[i], c = uc[i];
             const uint32_t S = sm.units.S[m], ch = sm.units.ch[m], keys = S + 1;
             const uint32_t k0 = c * ch, k1 = min(k0 + ch, keys);
             const float* Kc = arena_kv(a, sm.units, m, li, 0, h);
@@ -677,8 +685,8 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
                 Ls = fmaf(e, sm.vl[i][w], Ls);
                 O = fmaf(e, sm.vo[i][w][d], O);
             }
-            const uint32_t m = sm.um[i];
-            float* pp = a.part + (((size_t)m * kHeads + sm.uh[i]) * kMaxChunks + sm.uc[i]) * kPartStride;
+            const uint32_t m = um[i];
+            float* pp = a.part + (((size_t)m * kHeads + uh[i]) * kMaxChunks + uc[i]) * kPartStride;
             pp[4 + d] = O;
             if (d == 0) {
                 pp[0] = M;
@@ -687,16 +695,16 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
         }
         for (int tt = t; tt < np * 2 * kHeadDim; tt += kThreads) {
             const int i = tt / (2 * kHeadDim), r = tt % (2 * kHeadDim);
-            const uint32_t m = sm.um[i];
-            if (sm.uc[i] == sm.units.nch[m] - 1) {
-                float* dst = arena_kv(a, sm.units, m, li, r / kHeadDim, sm.uh[i]) + (size_t)sm.units.S[m] * kHeadDim;
+            const uint32_t m = um[i];
+            if (uc[i] == sm.units.nch[m] - 1) {
+                float* dst = arena_kv(a, sm.units, m, li, r / kHeadDim, uh[i]) + (size_t)sm.units.S[m] * kHeadDim;
                 dst[r % kHeadDim] = sm.qkvh[i][kHeadDim + r];
             }
         }
         csync();
         if (t < np) {
-            const uint32_t m = sm.um[t];
-            unsigned* cnt = a.head_cnt + ((size_t)li * kMaxBatch + m) * kHeads + sm.uh[t];
+            const uint32_t m = um[t];
+            unsigned* cnt = a.head_cnt + ((size_t)li * kMaxBatch + m) * kHeads + uh[t];
             unsigned old;
             asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
             const bool last = old == sm.units.nch[m] - 1;
@@ -707,7 +715,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
         if (t < np * kHeadDim) {  // last unit of (row, head): merge its partials in chunk order
             const int i = t / kHeadDim, d = t % kHeadDim;
             if (sm.last[i]) {
-                const uint32_t m = sm.um[i], h = sm.uh[i], nch = sm.units.nch[m];
+                const uint32_t m = um[i], h = uh[i], nch = sm.units.nch[m];
                 const float* ph = a.part + ((size_t)m * kHeads + h) * kMaxChunks * kPartStride;
                 float mv[kMaxChunks], lv[kMaxChunks], ov[kMaxChunks];
 #pragma unroll
@@ -732,6 +740,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
                 a.attn[(size_t)m * kWidth + h * kHeadDim + d] = O / Ls;
             }
         }
+        if (t < P) assign(base + (uint32_t)ncta * P, b ^ 1);  // the next pass's units (the other buffer)
         csync();
     }
 }
