@@ -628,6 +628,50 @@ def run_qwen(args):
     dec.close()
 
 
+def run_prefill_profile(args):
+    """One prefill of the config's first prefix (rows = its length) between
+    cudaProfilerStart/Stop, after three warm-up prefills, for
+    `ncu --profile-from-start off` captures of the prefill kernels; then five
+    CUDA-event timings of the same prefill.  --layers 2 uses a 2-layer
+    synthetic bundle (small captures) instead of the 24-layer bench model."""
+    import torch
+
+    torch.cuda.set_device(0)
+    gpt = importlib.import_module("index-tts-25-metal_b200.gpt")
+    mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+    path = bundle_path()
+    if args.layers != 24:
+        path = os.path.join(os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles"), f"gpt_s7_l{args.layers}_m0")
+        mit2.write_synthetic_gpt_bundle(path, seed=7, layers=args.layers, mask_stop=False)
+    dec = gpt.GptDecoder(path, device=0, weight_dtype=1 if args.weights == "bf16" else 0)
+    full = gpt.GptDecoder(bundle_path(), device=0) if args.layers != 24 else dec
+    prefix = build_workload(args.config, gpt, full, 0, 1)["prefixes"][0]
+    if full is not dec:
+        full.close()
+    rows = int(prefix.shape[0])
+    x = torch.from_numpy(prefix).cuda()
+    for _ in range(3):
+        dec.prefill_async(x.data_ptr(), rows)
+    dec.sync()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    dec.prefill_async(x.data_ptr(), rows)
+    dec.sync()
+    torch.cuda.profiler.stop()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    s = torch.cuda.ExternalStream(dec.stream)
+    ts = []
+    for _ in range(5):
+        ev[0].record(s)
+        dec.prefill_async(x.data_ptr(), rows)
+        ev[1].record(s)
+        dec.sync()
+        ts.append(ev[0].elapsed_time(ev[1]))
+    print(json.dumps({"prefill_profile": {"config": args.config, "rows": rows, "layers": args.layers,
+                                          "weights": args.weights, "ms": [round(t, 3) for t in ts]}}), flush=True)
+    dec.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,10 +689,15 @@ def main():
                     help="weight storage of the decoder (the headline is f32; bf16 is the optional weight path)")
     ap.add_argument("--codes", type=int, default=0,
                     help="override codes per request (profiler captures only; 0 = the config's own)")
+    ap.add_argument("--prefill-profile", action="store_true",
+                    help="profiler capture mode: one prefill of the config's prefix between cudaProfilerStart/Stop")
+    ap.add_argument("--layers", type=int, default=24, help="model depth for --prefill-profile (24 or a small model)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.prefill_profile:
+        run_prefill_profile(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     elif args.config == "qwen":
         run_qwen(args)
