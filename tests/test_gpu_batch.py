@@ -58,6 +58,19 @@ def test_batch_rows_equal_batch1_and_oracle(dec_masked, port_masked, gpt_mod, or
             np.testing.assert_array_equal(r.codes, e, err_msg=f"row {i} vs oracle")
 
 
+@pytest.mark.parametrize("lengths", [[236, 300, 420, 470], [520, 900, 35], [1000, 12, 700, 474, 230]])
+def test_batch_long_rows_equal_batch1(dec_masked, gpt_mod, lengths):
+    """Rows whose attention chunks hold 33-64 keys (two units' K/V loads per
+    round trip), more than 64 (one unit at a time) or a mix of both in one
+    pass: every row still gives the codes of its batch-1 decode."""
+    prefixes = ragged_prefixes(300 + len(lengths), lengths)
+    kws = [OPTION_MIX[(i + 2) % len(OPTION_MIX)] for i in range(len(lengths))]
+    res = dec_masked.generate_batch(prefixes, [gpt_mod.gen_opts(**k) for k in kws], 24)
+    for i, (p, k, r) in enumerate(zip(prefixes, kws, res)):
+        single = dec_masked.generate(p, gpt_mod.gen_opts(**k), 24)
+        np.testing.assert_array_equal(r.codes, single.codes, err_msg=f"row {i} (prefix {lengths[i]}) vs batch 1")
+
+
 def test_batch_bf16_rows_equal_batch1(gpt_mod, shallow_bf16_bundle):
     with gpt_mod.GptDecoder(shallow_bf16_bundle, weight_dtype=1) as dec:
         for batch in (2, 3, 8):
