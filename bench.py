@@ -628,6 +628,100 @@ def run_qwen(args):
     dec.close()
 
 
+CODEC_CPU_SCRIPT = r"""
+import json, sys, time
+sys.path.insert(0, {oracle!r})
+import numpy as np
+import oracle as O
+ref = O.RefCodec({bundle!r})
+codes = np.random.default_rng(7).integers(0, 8192, {n}).astype(np.uint32)
+ref.decode(codes[:8])
+t0 = time.perf_counter()
+ref.decode(codes)
+dt = time.perf_counter() - t0
+print(json.dumps({{"codes_per_s": {n} / dt, "threads": O.RefOracle.threads()}}))
+"""
+
+
+def codec_flops(T):
+    """Useful flops of one decode of T codes (codec.cpp:50-69): the embed conv
+    (k7, 1024 -> 384), 12 ConvNeXt blocks (depthwise k7, pwconv1 384 -> 2048,
+    pwconv2 2048 -> 384), the head linear 384 -> 1024 and the k3 conv
+    1024 -> 1024 over the 2T upsampled rows."""
+    D, F, H = 384, 2048, 1024
+    return (2 * T * D * H * 7 + 12 * (2 * T * D * 7 + 2 * T * F * D * 2) + 2 * T * H * D + 2 * (2 * T) * H * H * 3)
+
+
+def run_codec(args):
+    """Semantic codec decode (src/codec.cpp:50-69), the stage after the GPT:
+    the 1024 codes of a configs[1] request -> [2048, 1024] features.  value =
+    codes per second of device time (CUDA events around the decoder's
+    kernels); e2e = codes per second of the decode() call with host buffers;
+    roofline = useful flops over the device time against the measured bf16
+    tensor peak (the GEMMs run in fp32 on the CUDA cores; the nominal FP32
+    FFMA peak is reported beside it)."""
+    if env_int("RANK", 0) != 0:
+        return
+    gpt = importlib.import_module("index-tts-25-metal_b200.gpt")
+    mit2 = importlib.import_module("index-tts-25-metal_b200.mit2")
+    cache = os.environ.get("ITTS_BUNDLE_CACHE", "/tmp/itts_bundles")
+    path = os.path.join(cache, "codec_s43")
+    mit2.write_synthetic_codec_bundle(path, seed=43)
+    codec = gpt.SemanticCodec(path, device=env_int("LOCAL_RANK", 0))
+    n = args.codes or 1024
+    codes = np.random.default_rng(7).integers(0, 8192, n).astype(np.uint32)
+    for _ in range(args.warmup):
+        codec.decode(codes)
+    smi = ClockSampler(gpu_smi_id(env_int("LOCAL_RANK", 0)))
+    smi.start()
+    time.sleep(0.3)
+    dms, wall = [], 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        out = codec.decode(codes)
+        wall += time.perf_counter() - t0
+        dms.append(codec.last_timing().decode_ms)
+    clocks = smi.stop()
+    t = codec.last_timing()
+    fl = codec_flops(n)
+    achieved = fl / (statistics.mean(dms) / 1000.0) / 1e12
+    pk, pk_kind = peaks()
+    ffma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    cpu = None
+    if not args.no_cpu_baseline:
+        m = 64
+        code = CODEC_CPU_SCRIPT.format(oracle=os.path.join(ROOT, "oracle"), bundle=path, n=m)
+        try:
+            r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+            j = json.loads(r.stdout.strip().splitlines()[-1])
+            cpu = {"value": j["codes_per_s"], "unit": "codes/s", "cores": j["threads"], "kind": "reference",
+                   "sample": f"the reference's EnhancedCodec::decode (oracle/_ref) on the host: {m} codes"}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"unavailable": str(e)[:200]}
+    line = {
+        "metric": "semantic codec decode codes/s (codes -> 1024-d features)", "value": n / (statistics.mean(dms) / 1000.0),
+        "unit": "codes/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(dms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded random-init codec weights, seeded codes)",
+        "config": {"workload": f"semantic codec decode of {n} codes (a configs[1] request's output) into "
+                               f"[{2 * n}, 1024] features", "config": "codec",
+                   "l2": "activations of one decode fit in L2; weights 62 MB"},
+        "e2e": {"value": n * args.steps / wall, "unit": "codes/s", "h2d_bytes_per_step": int(codes.nbytes),
+                "d2h_bytes_per_step": int(out.nbytes)},
+        "gpu_launches": int(t.launches),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": float(pk["bf16_tflops"]), "unit": "TFLOP/s",
+                     "frac": achieved / float(pk["bf16_tflops"]), "traffic": None,
+                     "peak_source": f"{pk_kind} bf16_tflops", "kernel": "the decode's kernels (fp32 GEMMs dominate)",
+                     "algorithmic_flops_per_launch": fl, "avg_launch_ms": statistics.mean(dms),
+                     "fp32_ffma_peak_nominal_tflops": ffma_peak, "frac_of_ffma_peak": achieved / ffma_peak},
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    codec.close()
+
+
 def run_prefill_profile(args):
     """One prefill of the config's first prefix (rows = its length) between
     cudaProfilerStart/Stop, after three warm-up prefills, for
@@ -678,7 +772,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["0", "1", "2", "2beam", "3", "serving", "qwen"], default="1",
+    ap.add_argument("--config", choices=["0", "1", "2", "2beam", "3", "serving", "qwen", "codec"], default="1",
                     help="BASELINE.json workload (1 = the headline)")
     ap.add_argument("--rows", type=int, default=16, help="rows in flight for --config serving")
     ap.add_argument("--cpu-tokens", type=int, default=48)
@@ -701,6 +795,8 @@ def main():
         run_reference_arm(args)
     elif args.config == "qwen":
         run_qwen(args)
+    elif args.config == "codec":
+        run_codec(args)
     else:
         run_ours(args)
 

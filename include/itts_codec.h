@@ -33,8 +33,25 @@ const char* itts_codec_last_error(const itts_codec_ctx* ctx);
 
 /* EnhancedCodec::decode (codec.cpp:50-69): n codes (1 <= n <= 5000, each
  * < 8192; ITTS_ERR_INVALID_ARGUMENT otherwise) -> out[2n][1024] fp32
- * (out_floats >= 2n * 1024).  Synchronous. */
+ * (out_floats >= 2n * 1024).  Synchronous.  ITTS_ERR_DEVICE_TIMEOUT when a
+ * bounded wait of a tensor-core GEMM gave up (the context stays usable). */
 int itts_codec_decode(itts_codec_ctx* ctx, const uint32_t* codes, size_t n, float* out, size_t out_floats);
+
+/* GEMMs of the decode: 0 (default) the TMA-fed tcgen05 GEMM on TF32 hi / lo
+ * operands (three products, fp32 accuracy), 1 the fp32 CUDA-core tiles (kept
+ * for comparison).  No counterpart in the reference. */
+int itts_codec_set_gemm_mode(itts_codec_ctx* ctx, int mode);
+
+/* Device time of the last successful itts_codec_decode: CUDA events on the
+ * context's stream around the decoder's kernels (the code upload and the
+ * feature read excluded), the codes it decoded and the kernels it launched.
+ * No counterpart in the reference (measurement only). */
+typedef struct itts_codec_timing {
+    float decode_ms;
+    uint32_t codes;
+    uint32_t launches;
+} itts_codec_timing;
+int itts_codec_last_timing(const itts_codec_ctx* ctx, itts_codec_timing* out);
 
 #ifdef __cplusplus
 }

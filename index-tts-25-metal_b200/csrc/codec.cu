@@ -19,6 +19,8 @@
 // the GELU of pwconv1 and the layer scale + residual of pwconv2.  fp32 on the
 // CUDA cores, 64 x 64 tiles, k-tiles of 32; each output sums its K products in
 // k order.
+#include <vector>
+
 #include "codec.hpp"
 #include "common.cuh"
 
@@ -27,17 +29,6 @@ namespace {
 
 enum CodecLoad : int { kLoadPlain = 0, kLoadConv = 1, kLoadConvUp2 = 2 };
 enum CodecEpi : int { kCEpiBias = 0, kCEpiGelu = 1, kCEpiScaleResid = 2 };
-
-// GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from the Abramowitz-Stegun 7.1.26
-// rational approximation (max error 1.5e-7), the form of itts25_codec_gelu
-// (kernels.metal:3132-3137).
-__device__ __forceinline__ float gelu_erf(float x) {
-    const float v = x * 0.7071067811865475f, a = fabsf(v), t = 1.0f / (1.0f + 0.3275911f * a);
-    const float p = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    float erf = 1.0f - p * expf(-a * a);
-    if (v < 0.0f) erf = -erf;
-    return 0.5f * x * (1.0f + erf);
-}
 
 struct ConvSrc {
     const float* x;  // [rows, ch] source rows (before upsampling for kLoadConvUp2)
@@ -150,6 +141,8 @@ __global__ void k_codec_lookup(const uint32_t* __restrict__ codes, const float* 
                                const float* __restrict__ W, const float* __restrict__ b, float* __restrict__ out, int T) {
     const int t = blockIdx.x;
     __shared__ float e[8];
+    pdl_trigger();
+    pdl_wait();
     if (threadIdx.x < 8) e[threadIdx.x] = cb[(size_t)codes[t] * 8 + threadIdx.x];
     __syncthreads();
     for (int o = threadIdx.x; o < 1024; o += blockDim.x) {
@@ -164,8 +157,10 @@ __global__ void k_codec_lookup(const uint32_t* __restrict__ codes, const float* 
 // squared deviations (biased), eps inside the root (kernels.metal:618-669).
 __global__ void __launch_bounds__(128) k_codec_ln(const float* __restrict__ x, const float* __restrict__ g,
                                                   const float* __restrict__ be, float* __restrict__ out, int width,
-                                                  float eps) {
+                                                  float eps, float* __restrict__ out_lo = nullptr) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
     const float* row = x + (size_t)blockIdx.x * width;
     float v[8];
     float s = 0.f;
@@ -191,7 +186,35 @@ __global__ void __launch_bounds__(128) k_codec_ln(const float* __restrict__ x, c
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int c = threadIdx.x + 128 * j;
-        if (c < width) o[c] = (v[j] - mean) * inv * g[c] + be[c];
+        if (c < width) {
+            const float y = (v[j] - mean) * inv * g[c] + be[c];
+            if (out_lo) {  // split for the tensor-core GEMM: y = hi + lo
+                const float hi = rn_tf32(y);
+                o[c] = hi;
+                out_lo[(size_t)blockIdx.x * width + c] = rn_tf32(y - hi);
+            } else {
+                o[c] = y;
+            }
+        }
+    }
+}
+
+// im2col of a same-padded convolution over time, split into TF32 hi / lo for
+// the tensor-core GEMM: row t, column c * ks + j holds x[t + j - ks/2][c]
+// (zero outside [0, rows_out)), read from the nearest x2 upsampled rows
+// x[floor(s / 2)] when up2 (the A operand load_a computes on the fly).
+__global__ void k_codec_im2col(const float* __restrict__ x, int ch, int ks, int rows_out, int up2,
+                               float* __restrict__ hi, float* __restrict__ lo) {
+    const size_t width = (size_t)ch * ks, n = (size_t)rows_out * width;
+    pdl_trigger();
+    pdl_wait();
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const int t = int(e / width), kk = int(e % width), c = kk / ks, j = kk - c * ks;
+        const int s = t + j - ks / 2;
+        const float v = s >= 0 && s < rows_out ? x[(size_t)(up2 ? s >> 1 : s) * ch + c] : 0.0f;
+        const float h = rn_tf32(v);
+        hi[e] = h;
+        lo[e] = rn_tf32(v - h);
     }
 }
 
@@ -199,6 +222,8 @@ __global__ void __launch_bounds__(128) k_codec_ln(const float* __restrict__ x, c
 __global__ void k_codec_dwconv(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                                float* __restrict__ out, int T, int ch, int ks) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
     if (c >= ch) return;
     float acc = 0.f;
     for (int j = 0; j < ks; ++j) {
@@ -218,15 +243,144 @@ cudaError_t gemm(const float* A, ConvSrc cs, const float* W, const float* bias, 
 
 }  // namespace
 
+namespace {
+
+constexpr int kD = 384, kF = 2048, kH = 1024;
+
+// Tensor maps of the split activations for T rows (re-encoded when T changes;
+// the block grows to the largest T seen).
+cudaError_t codec_tc_rows(CodecTc* tc, int T) {
+    if (tc->rows == T) return cudaSuccess;
+    const size_t per_row = size_t(kH) * 7 + kD + kF + 2 * size_t(kH) * 3;  // col_e, ln, u, col_u (2 rows)
+    cudaError_t e;
+    if (T > tc->act_cap) {
+        if (tc->act) cudaFree(tc->act);
+        tc->act = nullptr;
+        tc->act_cap = 0;
+        if ((e = cudaMalloc(&tc->act, 2 * per_row * size_t(T) * sizeof(float))) != cudaSuccess) return e;
+        tc->act_cap = T;
+    }
+    float* p = tc->act;
+    auto take = [&](float* (&pair)[2], size_t n) {
+        pair[0] = p;
+        pair[1] = p + n;
+        p += 2 * n;
+    };
+    const size_t cap = size_t(tc->act_cap);
+    take(tc->col_e, cap * kH * 7);
+    take(tc->ln, cap * kD);
+    take(tc->u, cap * kF);
+    take(tc->col_u, 2 * cap * kH * 3);
+    for (int h = 0; h < 2; ++h) {
+        if ((e = tma_make_map(&tc->a_col_e[h], tc->col_e[h], T, kH * 7)) != cudaSuccess ||
+            (e = tma_make_map(&tc->a_ln[h], tc->ln[h], T, kD)) != cudaSuccess ||
+            (e = tma_make_map(&tc->a_u[h], tc->u[h], T, kF)) != cudaSuccess ||
+            (e = tma_make_map(&tc->a_col_u[h], tc->col_u[h], 2 * T, kH * 3)) != cudaSuccess)
+            return e;
+    }
+    tc->rows = T;
+    return cudaSuccess;
+}
+
+cudaError_t tc_gemm(CodecTc* tc, const TmaMap* a, const TmaMap* w, int epi, const float* bias, const float* R,
+                    const float* gamma, float* C, float* C_lo, int M, int N, int K, cudaStream_t s) {
+    TmaGemm g{a, w, bias, R, C, C_lo, M, N, K, epi, tc->ws, tc->counters, kCodecCounters, tc->status, gamma};
+    return tma_gemm(g, s);
+}
+
+}  // namespace
+
+cudaError_t codec_tc_init(CodecTc* tc, const CodecWeights& w, cudaStream_t s) {
+    struct Mat {
+        const float* src;
+        int rows, cols;
+        TmaMap* maps;
+    };
+    std::vector<Mat> mats;
+    mats.push_back({w.embed_w, kD, kH * 7, tc->w_embed});
+    for (int i = 0; i < 12; ++i) {
+        mats.push_back({w.block[i].pw1_w, kF, kD, tc->w_pw1[i]});
+        mats.push_back({w.block[i].pw2_w, kD, kF, tc->w_pw2[i]});
+    }
+    mats.push_back({w.head_w, kH, kD, tc->w_head});
+    mats.push_back({w.up_w, kH, kH * 3, tc->w_up});
+    size_t total = 0;
+    for (const Mat& m : mats) total += 2 * size_t(m.rows) * m.cols;
+    cudaError_t e;
+    if ((e = cudaMalloc(&tc->wsplit, total * sizeof(float))) != cudaSuccess) return e;
+    float* p = tc->wsplit;
+    for (const Mat& m : mats) {
+        const size_t n = size_t(m.rows) * m.cols;
+        if ((e = tma_split(m.src, p, p + n, n, s)) != cudaSuccess ||
+            (e = tma_make_map(&m.maps[0], p, m.rows, m.cols)) != cudaSuccess ||
+            (e = tma_make_map(&m.maps[1], p + n, m.rows, m.cols)) != cudaSuccess)
+            return e;
+        p += 2 * n;
+    }
+    if ((e = cudaMalloc(&tc->ws, tma_workspace_floats() * sizeof(float))) != cudaSuccess ||
+        (e = cudaMalloc(&tc->counters, (kCodecCounters + 1) * sizeof(int))) != cudaSuccess)
+        return e;
+    tc->status = tc->counters + kCodecCounters;
+    if ((e = cudaMemsetAsync(tc->counters, 0, (kCodecCounters + 1) * sizeof(int), s)) != cudaSuccess) return e;
+    return cudaStreamSynchronize(s);
+}
+
+void codec_tc_free(CodecTc* tc) {
+    for (void* p : {(void*)tc->wsplit, (void*)tc->act, (void*)tc->ws, (void*)tc->counters})
+        if (p) cudaFree(p);
+    *tc = CodecTc{};
+}
+
 // The decode of T codes (host-validated: 1 <= T <= 5000, codes < 8192) on
 // stream s; out receives [2T, 1024].
-cudaError_t codec_decode_device(const CodecWeights& w, const CodecScratch& sc, const uint32_t* d_codes, int T,
-                                float* out, cudaStream_t s) {
-    constexpr int D = 384, F = 2048, H = 1024;
+cudaError_t codec_decode_device(const CodecWeights& w, const CodecScratch& sc, CodecTc* tc, const uint32_t* d_codes,
+                                int T, float* out, cudaStream_t s) {
+    constexpr int D = kD, F = kF, H = kH;
     const ConvSrc none{nullptr, 0, 1, 0};
     cudaError_t e;
     k_codec_lookup<<<T, 256, 0, s>>>(d_codes, w.codebook, w.out_w, w.out_b, sc.hidden, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (tc) {
+        // tensor-core GEMMs (TF32 hi / lo, three products): the activations
+        // that feed a GEMM are written split by the kernel producing them
+        if ((e = codec_tc_rows(tc, T)) != cudaSuccess) return e;
+        // a CTA that gave up leaves its tile's counter behind
+        if ((e = cudaMemsetAsync(tc->counters, 0, kCodecCounters * sizeof(int), s)) != cudaSuccess) return e;
+        // every kernel of this chain is launched with PDL (it waits for its
+        // predecessor before touching the buffers they share)
+        const int grid = 148 * 8;
+        float* none_lo = nullptr;
+        if ((e = launch_pdl(k_codec_im2col, dim3(grid), 256, 0, s, (const float*)sc.hidden, H, 7, T, 0, tc->col_e[0],
+                            tc->col_e[1])) != cudaSuccess ||
+            (e = tc_gemm(tc, tc->a_col_e, tc->w_embed, TmaEpiBias, w.embed_b, nullptr, nullptr, sc.h, nullptr, T, D,
+                         H * 7, s)) != cudaSuccess ||
+            (e = launch_pdl(k_codec_ln, dim3(T), 128, 0, s, (const float*)sc.h, w.norm_g, w.norm_b, sc.x, D, 1e-6f,
+                            none_lo)) != cudaSuccess)
+            return e;
+        for (int i = 0; i < 12; ++i) {
+            const CodecBlockW& bw = w.block[i];
+            if ((e = launch_pdl(k_codec_dwconv, dim3((D + 127) / 128, T), 128, 0, s, (const float*)sc.x, bw.dw_w,
+                                bw.dw_b, sc.h, T, D, 7)) != cudaSuccess ||
+                (e = launch_pdl(k_codec_ln, dim3(T), 128, 0, s, (const float*)sc.h, bw.ln_g, bw.ln_b, tc->ln[0], D,
+                                1e-6f, tc->ln[1])) != cudaSuccess)
+                return e;
+            if ((e = tc_gemm(tc, tc->a_ln, tc->w_pw1[i], TmaEpiGeluErf, bw.pw1_b, nullptr, nullptr, tc->u[0],
+                             tc->u[1], T, F, D, s)) != cudaSuccess ||
+                (e = tc_gemm(tc, tc->a_u, tc->w_pw2[i], TmaEpiScaleResid, bw.pw2_b, sc.x, bw.gamma, sc.x, nullptr, T,
+                             D, F, s)) != cudaSuccess)
+                return e;
+        }
+        if ((e = launch_pdl(k_codec_ln, dim3(T), 128, 0, s, (const float*)sc.x, w.final_g, w.final_b, tc->ln[0], D,
+                            1e-6f, tc->ln[1])) != cudaSuccess ||
+            (e = tc_gemm(tc, tc->a_ln, tc->w_head, TmaEpiBias, w.head_b, nullptr, nullptr, sc.hidden, nullptr, T, H,
+                         D, s)) != cudaSuccess ||
+            (e = launch_pdl(k_codec_im2col, dim3(grid), 256, 0, s, (const float*)sc.hidden, H, 3, 2 * T, 1,
+                            tc->col_u[0], tc->col_u[1])) != cudaSuccess)
+            return e;
+        return tc_gemm(tc, tc->a_col_u, tc->w_up, TmaEpiBias, w.up_b, nullptr, nullptr, out, nullptr, 2 * T, H,
+                       H * 3, s);
+    }
+    // CUDA-core GEMMs
     // embed conv k=7 1024 -> 384, LayerNorm
     if ((e = gemm<kLoadConv, kCEpiBias>(nullptr, ConvSrc{sc.hidden, H, 7, T}, w.embed_w, w.embed_b, nullptr, nullptr,
                                         sc.h, T, D, H * 7, s)) != cudaSuccess)

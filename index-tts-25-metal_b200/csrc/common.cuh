@@ -157,6 +157,17 @@ __device__ __forceinline__ float gelu_ref(float v) {
     return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
 }
 
+// GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from the Abramowitz-Stegun 7.1.26
+// rational approximation (max error 1.5e-7), the form of itts25_codec_gelu
+// (kernels.metal:3132-3137).
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float v = x * 0.7071067811865475f, a = fabsf(v), t = 1.0f / (1.0f + 0.3275911f * a);
+    const float p = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    float erf = 1.0f - p * expf(-a * a);
+    if (v < 0.0f) erf = -erf;
+    return 0.5f * x * (1.0f + erf);
+}
+
 // Programmatic dependent launch (PDL).  A kernel launched with programmatic
 // stream serialization may start while its predecessor in the stream drains:
 // it does what does not depend on it (setup, weight loads), waits for it with

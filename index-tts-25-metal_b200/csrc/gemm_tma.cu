@@ -169,9 +169,17 @@ struct GemmArgs {
     float* ws;       // partial tiles: two 128 x 128 slots per CTA (its first and its last tile)
     int* counters;   // per output tile: contributors that have stored their partial (the last resets)
     int* status;
+    const float* gamma;  // layer scale [N] (kEpiScaleResid)
 };
 
-enum GemmEpi : int { kEpiBias = TmaEpiBias, kEpiGelu = TmaEpiGelu, kEpiResid = TmaEpiResid, kEpiSwiGLU = TmaEpiSwiGLU };
+enum GemmEpi : int {
+    kEpiBias = TmaEpiBias,
+    kEpiGelu = TmaEpiGelu,
+    kEpiResid = TmaEpiResid,
+    kEpiSwiGLU = TmaEpiSwiGLU,
+    kEpiGeluErf = TmaEpiGeluErf,
+    kEpiScaleResid = TmaEpiScaleResid
+};
 
 // CTA i owns units [i U / G, (i + 1) U / G) of the tile-major (tile, K block)
 // sequence: every CTA gets the same number of K blocks (to one), whatever the
@@ -209,8 +217,11 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int m, int n, float
         return;
     }
     const size_t o = size_t(m) * g.N + n;
-    if (EPI == kEpiGelu) {
-        y = make_float4(gelu_ref(y.x), gelu_ref(y.y), gelu_ref(y.z), gelu_ref(y.w));
+    if (EPI == kEpiGelu || EPI == kEpiGeluErf) {
+        if (EPI == kEpiGelu)
+            y = make_float4(gelu_ref(y.x), gelu_ref(y.y), gelu_ref(y.z), gelu_ref(y.w));
+        else
+            y = make_float4(gelu_erf(y.x), gelu_erf(y.y), gelu_erf(y.z), gelu_erf(y.w));
         if (g.C_lo) {
             const float4 h = make_float4(rn_tf32(y.x), rn_tf32(y.y), rn_tf32(y.z), rn_tf32(y.w));
             *reinterpret_cast<float4*>(g.C + o) = h;
@@ -221,6 +232,10 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int m, int n, float
     } else if (EPI == kEpiResid) {
         const float4 r = *reinterpret_cast<const float4*>(g.R + o);
         y = make_float4(r.x + y.x, r.y + y.y, r.z + y.z, r.w + y.w);
+    } else if (EPI == kEpiScaleResid) {  // x + gamma * pwconv2(.) (codec.cpp:46); R may alias C
+        const float4 r = *reinterpret_cast<const float4*>(g.R + o);
+        const float4 s = __ldg(reinterpret_cast<const float4*>(g.gamma + n));
+        y = make_float4(fmaf(y.x, s.x, r.x), fmaf(y.y, s.y, r.y), fmaf(y.z, s.z, r.z), fmaf(y.w, s.w, r.w));
     }
     *reinterpret_cast<float4*>(g.C + o) = y;
 }
@@ -668,7 +683,7 @@ namespace {
 // One GEMM C = epi(A W^T + bias) from A's and W's (hi, lo) tensor maps.
 cudaError_t run_gemm(const CUtensorMap* ma, const CUtensorMap* mw, int epi, const float* bias, const float* R,
                      float* C, float* C_lo, int M, int N, int K, float* ws, int* counters, int counters_n,
-                     int* status, cudaStream_t s) {
+                     int* status, cudaStream_t s, const float* gamma = nullptr) {
     if (M < 1 || N % GN || K % GK || K < GK) return cudaErrorInvalidValue;
     const int kbt = K / GK, tiles = ((M + GM - 1) / GM) * (N / GN);
     if (tiles > counters_n) return cudaErrorInvalidValue;
@@ -678,10 +693,12 @@ cudaError_t run_gemm(const CUtensorMap* ma, const CUtensorMap* mw, int epi, cons
     const long long units = (long long)tiles * kbt;
     const int ctas = int(std::max(1LL, std::min({(long long)std::min(sm_count(), kMaxCtas),
                                                  (long long)kCtasPerTile * tiles, units / kChunk})));
-    GemmArgs g{bias, R, C, C_lo, M, N, K, kbt, N / GN, ctas, units, ws, counters, status};
+    GemmArgs g{bias, R, C, C_lo, M, N, K, kbt, N / GN, ctas, units, ws, counters, status, gamma};
     switch (epi) {
         case kEpiGelu: return launch_epi<kEpiGelu>(ma, mw, g, s);
         case kEpiResid: return launch_epi<kEpiResid>(ma, mw, g, s);
+        case kEpiGeluErf: return launch_epi<kEpiGeluErf>(ma, mw, g, s);
+        case kEpiScaleResid: return R && gamma ? launch_epi<kEpiScaleResid>(ma, mw, g, s) : cudaErrorInvalidValue;
         case kEpiSwiGLU: return C_lo ? launch_epi<kEpiSwiGLU>(ma, mw, g, s) : cudaErrorInvalidValue;
         default: return launch_epi<kEpiBias>(ma, mw, g, s);
     }
@@ -725,7 +742,7 @@ cudaError_t tma_gemm(const TmaGemm& q, cudaStream_t s) {
     std::memcpy(ma, q.a, sizeof ma);
     std::memcpy(mw, q.w, sizeof mw);
     return run_gemm(ma, mw, q.epi, q.bias, q.R, q.C, q.C_lo, q.M, q.N, q.K, q.ws, q.counters, q.counters_n,
-                    q.status, s);
+                    q.status, s, q.gamma);
 }
 
 }  // namespace itts

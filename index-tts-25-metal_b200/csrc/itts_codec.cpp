@@ -48,12 +48,19 @@ struct itts_codec_ctx {
     uint32_t* d_codes = nullptr;
     float* d_out = nullptr;
     size_t out_tokens = 0;
+    cudaEvent_t ev[2] = {nullptr, nullptr};  // around the kernels of a decode
+    itts_codec_timing timing{};
+    itts::CodecTc tc;  // tensor-core GEMM state
+    int gemm_mode = 0; // 0: tensor-core GEMMs, 1: CUDA-core GEMMs
 
     ~itts_codec_ctx() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         for (void* p : {(void*)d_weights, (void*)d_scratch, (void*)d_codes, (void*)d_out})
             if (p) cudaFree(p);
+        for (cudaEvent_t e : ev)
+            if (e) cudaEventDestroy(e);
+        itts::codec_tc_free(&tc);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -225,6 +232,7 @@ int itts_codec_create(const char* bundle_dir, int device, itts_codec_ctx** out) 
         cck(cudaSetDevice(device), "cudaSetDevice");
         cck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream creation");
         upload(c.get(), bundle);
+        cck(itts::codec_tc_init(&c->tc, c->w, c->stream), "tensor-core GEMM setup");
     });
     if (rc != ITTS_OK) {
         g_codec_create_error = c->err;
@@ -246,12 +254,44 @@ int itts_codec_decode(itts_codec_ctx* ctx, const uint32_t* codes, size_t n, floa
         if (bad) cfail(ITTS_ERR_INVALID_ARGUMENT, "Codec expects 1..5000 code IDs in [0,8192)");
         if (!out || out_floats < 2 * n * 1024) cfail(ITTS_ERR_INVALID_ARGUMENT, "output buffer too small");
         ensure_scratch(ctx, n);
+        if (!ctx->ev[0]) {
+            cck(cudaEventCreate(&ctx->ev[0]), "event creation");
+            cck(cudaEventCreate(&ctx->ev[1]), "event creation");
+        }
         cck(cudaMemcpyAsync(ctx->d_codes, codes, n * 4, cudaMemcpyHostToDevice, ctx->stream), "code upload");
-        cck(itts::codec_decode_device(ctx->w, ctx->sc, ctx->d_codes, int(n), ctx->d_out, ctx->stream),
+        cck(cudaEventRecord(ctx->ev[0], ctx->stream), "event record");
+        const bool tc = ctx->gemm_mode == 0;
+        cck(itts::codec_decode_device(ctx->w, ctx->sc, tc ? &ctx->tc : nullptr, ctx->d_codes, int(n), ctx->d_out,
+                                      ctx->stream),
             "codec decode launch");
+        cck(cudaEventRecord(ctx->ev[1], ctx->stream), "event record");
         cck(cudaMemcpyAsync(out, ctx->d_out, 2 * n * 1024 * 4, cudaMemcpyDeviceToHost, ctx->stream), "features read");
+        int status = 0;
+        if (tc) cck(cudaMemcpyAsync(&status, ctx->tc.status, sizeof status, cudaMemcpyDeviceToHost, ctx->stream),
+                    "status read");
         cck(cudaStreamSynchronize(ctx->stream), "codec decode");
+        if (status) {  // a GEMM wait gave up: the features are not valid
+            cck(cudaMemsetAsync(ctx->tc.status, 0, sizeof status, ctx->stream), "status clear");
+            cck(cudaStreamSynchronize(ctx->stream), "status clear");
+            cfail(ITTS_ERR_DEVICE_TIMEOUT, "codec GEMM device wait timed out (status " + std::to_string(status) + ")");
+        }
+        float ms = 0.f;
+        cck(cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]), "event time");
+        ctx->timing =
+            itts_codec_timing{ms, uint32_t(n), uint32_t(tc ? itts::kCodecLaunchesTc : itts::kCodecLaunches)};
     });
+}
+
+int itts_codec_set_gemm_mode(itts_codec_ctx* ctx, int mode) {
+    if (!ctx || mode < 0 || mode > 1) return ITTS_ERR_INVALID_ARGUMENT;
+    ctx->gemm_mode = mode;
+    return ITTS_OK;
+}
+
+int itts_codec_last_timing(const itts_codec_ctx* ctx, itts_codec_timing* out) {
+    if (!ctx || !out) return ITTS_ERR_INVALID_ARGUMENT;
+    *out = ctx->timing;
+    return ITTS_OK;
 }
 
 }  // extern "C"

@@ -216,6 +216,8 @@ enum TmaEpi : int {
     TmaEpiGelu = 1,    // GELU (GPT-2 tanh form); with C_lo the output is split hi / lo
     TmaEpiResid = 2,   // C = R + A W^T + bias
     TmaEpiSwiGLU = 3,  // W rows interleave gate / up: C, C_lo [M][N/2] = split(silu(gate) * up)
+    TmaEpiGeluErf = 4,     // GELU (erf form of the codec); with C_lo the output is split hi / lo
+    TmaEpiScaleResid = 5,  // C = R + (A W^T + bias) * gamma (layer scale + residual)
 };
 struct TmaMap {
     alignas(64) unsigned char bytes[128];
@@ -232,6 +234,7 @@ struct TmaGemm {
     int* counters;     // >= output tiles, zeroed
     int counters_n;
     int* status;
+    const float* gamma = nullptr;  // [N] layer scale (TmaEpiScaleResid)
 };
 cudaError_t tma_make_map(TmaMap* m, const float* base, uint64_t rows, uint64_t cols);
 cudaError_t tma_split(const float* src, float* hi, float* lo, size_t n, cudaStream_t s);

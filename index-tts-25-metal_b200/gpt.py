@@ -111,6 +111,8 @@ SIGNATURES = {
     "itts_qwen_generate": (C.c_int, [_P, _P, C.c_size_t, C.c_uint32, _P, C.c_size_t, C.POINTER(C.c_uint32)]),
     "itts_qwen_cached_tokens": (C.c_uint32, [_P]),
     "itts_qwen_last_timing": (C.c_int, [_P, _P]),
+    "itts_codec_last_timing": (C.c_int, [_P, _P]),
+    "itts_codec_set_gemm_mode": (C.c_int, [_P, C.c_int]),
 }
 
 _lib = None
@@ -413,6 +415,22 @@ class SemanticCodec:
         if rc != OK:
             _raise(rc, self._lib.itts_codec_last_error(self._h).decode())
         return out[:2 * c.size]
+
+    def set_gemm_mode(self, mode: int):
+        """0: tensor-core GEMMs (default), 1: fp32 CUDA-core GEMMs."""
+        if self._lib.itts_codec_set_gemm_mode(self._h, mode) != OK:
+            raise ValueError("codec GEMM mode is 0 or 1")
+
+    def last_timing(self) -> "CodecTiming":
+        t = CodecTiming()
+        rc = self._lib.itts_codec_last_timing(self._h, C.byref(t))
+        if rc != OK:
+            _raise(rc, "codec timing")
+        return t
+
+
+class CodecTiming(C.Structure):
+    _fields_ = [("decode_ms", C.c_float), ("codes", C.c_uint32), ("launches", C.c_uint32)]
 
 
 QWEN_VOCAB = 151936

@@ -62,6 +62,38 @@ def test_codec_decode_matches_live_reference(codec, codec_bundle, oracle_mod):
     assert_features_close(codec.decode(g["short.codes"]), g["short.features"], "17 codes after 300")
 
 
+def test_codec_gemm_modes_match_reference(codec, codec_bundle, oracle_mod):
+    """Both GEMM paths (0: tcgen05 on TF32 hi / lo operands, the default; 1:
+    fp32 CUDA-core tiles) against the fixture, and at 1100 codes (9 row tiles
+    of the stream-K GEMMs, 2200 rows for the up conv) against the live
+    reference; the timing record counts each path's launches."""
+    g = golden("codec.npz")
+    codes = np.random.default_rng(78).integers(0, 8192, 1100).astype(np.uint32)
+    want = None
+    if oracle_mod.RefOracle.available():
+        ref = oracle_mod.RefCodec(codec_bundle)
+        try:
+            want = ref.decode(codes)
+        finally:
+            ref.close()
+    got = {}
+    try:
+        for mode, launches in ((0, 56), (1, 54)):
+            codec.set_gemm_mode(mode)
+            for name in ("one", "short"):
+                assert_features_close(codec.decode(g[f"{name}.codes"]), g[f"{name}.features"], f"mode {mode} {name}")
+            got[mode] = codec.decode(codes)
+            t = codec.last_timing()
+            assert t.codes == 1100 and t.launches == launches and t.decode_ms > 0
+            if want is not None:
+                assert_features_close(got[mode], want, f"mode {mode} 1100 codes")
+    finally:
+        codec.set_gemm_mode(0)
+    assert_features_close(got[0], got[1], "tensor-core vs CUDA-core GEMMs")
+    with pytest.raises(ValueError):
+        codec.set_gemm_mode(2)
+
+
 def test_codec_rejects_what_the_reference_rejects(codec, gpt_mod):
     for bad in (np.array([], np.uint32), np.array([8192], np.uint32), np.zeros(5001, np.uint32)):
         with pytest.raises(ValueError, match=r"Codec expects 1\.\.5000 code IDs in \[0,8192\)"):
