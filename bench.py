@@ -658,8 +658,9 @@ def run_codec(args):
     codes per second of device time (CUDA events around the decoder's
     kernels); e2e = codes per second of the decode() call with host buffers;
     roofline = useful flops over the device time against the measured bf16
-    tensor peak (the GEMMs run in fp32 on the CUDA cores; the nominal FP32
-    FFMA peak is reported beside it)."""
+    tensor peak (the GEMMs run on the tensor cores as three TF32 products per
+    term, so the useful rate is at most a third of it; the nominal FP32 FFMA
+    peak, the CUDA-core alternative, is reported beside it)."""
     if env_int("RANK", 0) != 0:
         return
     gpt = importlib.import_module("index-tts-25-metal_b200.gpt")
@@ -711,7 +712,7 @@ def run_codec(args):
         "gpu_launches": int(t.launches),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": float(pk["bf16_tflops"]), "unit": "TFLOP/s",
                      "frac": achieved / float(pk["bf16_tflops"]), "traffic": None,
-                     "peak_source": f"{pk_kind} bf16_tflops", "kernel": "the decode's kernels (fp32 GEMMs dominate)",
+                     "peak_source": f"{pk_kind} bf16_tflops", "kernel": "the decode's 56 kernels (27 TF32 hi/lo tcgen05 GEMMs dominate)",
                      "algorithmic_flops_per_launch": fl, "avg_launch_ms": statistics.mean(dms),
                      "fp32_ffma_peak_nominal_tflops": ffma_peak, "frac_of_ffma_peak": achieved / ffma_peak},
         "clocks": clocks,
