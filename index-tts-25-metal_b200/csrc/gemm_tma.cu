@@ -691,8 +691,12 @@ cudaError_t run_gemm(const CUtensorMap* ma, const CUtensorMap* mw, int epi, cons
     // one accumulation chunk per CTA, and few tiles spread over at most
     // kCtasPerTile CTAs each.
     const long long units = (long long)tiles * kbt;
-    const int ctas = int(std::max(1LL, std::min({(long long)std::min(sm_count(), kMaxCtas),
-                                                 (long long)kCtasPerTile * tiles, units / kChunk})));
+    const int sms = std::min(sm_count(), kMaxCtas);
+    int ctas = int(std::max(1LL, std::min({(long long)sms, (long long)kCtasPerTile * tiles, units / kChunk})));
+    // Between 3/4 of the SMs and all of them in tiles, one CTA per tile: no
+    // tile is split, so no partial goes through the workspace (measured: 451-row
+    // prefill 5.81 -> 5.61 ms, 1024-code codec decode 0.955 -> 0.880 ms).
+    if (tiles <= sms && tiles * 4 >= sms * 3) ctas = tiles;
     GemmArgs g{bias, R, C, C_lo, M, N, K, kbt, N / GN, ctas, units, ws, counters, status, gamma};
     switch (epi) {
         case kEpiGelu: return launch_epi<kEpiGelu>(ma, mw, g, s);
