@@ -168,6 +168,20 @@ __device__ __forceinline__ float gelu_erf(float x) {
     return 0.5f * x * (1.0f + erf);
 }
 
+// Two independent fp32 fused multiply-adds (round to nearest even, as fmaf)
+// in one instruction: (a.x * b.x + c.x, a.y * b.y + c.y).  Each lane of the
+// pair is exactly fmaf of its operands, so a kernel issuing these for two
+// independent fma chains computes the same values with half the FMA issue.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // Programmatic dependent launch (PDL).  A kernel launched with programmatic
 // stream serialization may start while its predecessor in the stream drains:
 // it does what does not depend on it (setup, weight loads), waits for it with

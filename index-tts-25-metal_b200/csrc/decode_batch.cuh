@@ -156,13 +156,10 @@ __device__ __forceinline__ void row_dots(const wtype* wrow, const float2 (&x)[kM
     for (int j = 0; j < kVec; ++j) wv[j] = w[j * 32];
 #pragma unroll
     for (int mm = 0; mm < kMPG; ++mm) {
-        float a0 = 0.f, a1 = 0.f;
+        float2 a = make_float2(0.f, 0.f);  // the two chains (a0, a1), one paired fma per step
 #pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            a0 = fmaf(wv[j].x, x[mm][j].x, a0);
-            a1 = fmaf(wv[j].y, x[mm][j].y, a1);
-        }
-        acc[mm] = a0 + a1;
+        for (int j = 0; j < kVec; ++j) a = fma2(wv[j], x[mm][j], a);
+        acc[mm] = a.x + a.y;
     }
 #endif
 }
