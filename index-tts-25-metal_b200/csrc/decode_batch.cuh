@@ -138,16 +138,14 @@ __device__ __forceinline__ void row_dots(const wtype* wrow, const float2 (&x)[kM
     for (int j = 0; j < kVec; j += 2) raw[j >> 1] = w[(j >> 1) * 32];
 #pragma unroll
     for (int mm = 0; mm < kMPG; ++mm) {
-        float a0 = 0.f, a1 = 0.f;
+        float2 a = make_float2(0.f, 0.f);  // the two chains (a0, a1), one paired fma per step
 #pragma unroll
         for (int j = 0; j < kVec; j += 2) {
             const uint2 r = raw[j >> 1];
-            a0 = fmaf(__uint_as_float(r.x << 16), x[mm][j].x, a0);
-            a1 = fmaf(__uint_as_float(r.x & 0xffff0000u), x[mm][j].y, a1);
-            a0 = fmaf(__uint_as_float(r.y << 16), x[mm][j + 1].x, a0);
-            a1 = fmaf(__uint_as_float(r.y & 0xffff0000u), x[mm][j + 1].y, a1);
+            a = fma2(make_float2(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u)), x[mm][j], a);
+            a = fma2(make_float2(__uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u)), x[mm][j + 1], a);
         }
-        acc[mm] = a0 + a1;
+        acc[mm] = a.x + a.y;
     }
 #else
     float2 wv[kVec];
@@ -536,8 +534,7 @@ __device__ __forceinline__ void battn_vw_packed(const BatchArgs& a, int li, BAtt
                 const float p = expf(sk[ii] - mn);
                 const float2 v = ii < W ? vv[r * W + ii] : make_float2(0.f, 0.f);
                 l += p;
-                o.x = fmaf(p, v.x, o.x);
-                o.y = fmaf(p, v.y, o.y);
+                o = fma2(make_float2(p, p), v, o);
             }
             mx = mn;
         }
@@ -655,8 +652,7 @@ __device__ void battn_phase(const BatchArgs& a, int li, uint32_t act, uint32_t g
                 for (int ii = 0; ii < kKB; ++ii) {
                     const float p = expf(sk[ii] - mn);
                     l += p;
-                    o.x = fmaf(p, vv[ii].x, o.x);
-                    o.y = fmaf(p, vv[ii].y, o.y);
+                    o = fma2(make_float2(p, p), vv[ii], o);
                 }
                 mx = mn;
             }
