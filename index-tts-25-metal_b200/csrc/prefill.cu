@@ -267,11 +267,15 @@ __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ q
         for (int d = 0; d < 64; ++d) {
             const float4 qv = *reinterpret_cast<const float4*>(QT + d * kAttLd + 4 * ty);
             const float4 kv = *reinterpret_cast<const float4*>(KT + d * kAttLd + 4 * tx);
-            const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, kb[4] = {kv.x, kv.y, kv.z, kv.w};
+            const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+            const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qa[a], kb[b], sc[a][b]);
+            for (int a = 0; a < 4; ++a) {  // paired fmas: each half is fmaf(qa[a], kb[b], sc[a][b])
+                const float2 q2 = make_float2(qa[a], qa[a]);
+                const float2 s01 = fma2(q2, k01, make_float2(sc[a][0], sc[a][1]));
+                const float2 s23 = fma2(q2, k23, make_float2(sc[a][2], sc[a][3]));
+                sc[a][0] = s01.x, sc[a][1] = s01.y, sc[a][2] = s23.x, sc[a][3] = s23.y;
+            }
         }
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
@@ -311,11 +315,11 @@ __global__ void __launch_bounds__(256) k_causal_attn(const float* __restrict__ q
             for (int a = 0; a < 4; ++a) {
                 const float p4[4] = {pr[a].x, pr[a].y, pr[a].z, pr[a].w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[a][0] = fmaf(p4[i], vr[i].x, acc[a][0]);
-                    acc[a][1] = fmaf(p4[i], vr[i].y, acc[a][1]);
-                    acc[a][2] = fmaf(p4[i], vr[i].z, acc[a][2]);
-                    acc[a][3] = fmaf(p4[i], vr[i].w, acc[a][3]);
+                for (int i = 0; i < 4; ++i) {  // paired fmas, each half fmaf(p, v, acc)
+                    const float2 p2 = make_float2(p4[i], p4[i]);
+                    const float2 a01 = fma2(p2, make_float2(vr[i].x, vr[i].y), make_float2(acc[a][0], acc[a][1]));
+                    const float2 a23 = fma2(p2, make_float2(vr[i].z, vr[i].w), make_float2(acc[a][2], acc[a][3]));
+                    acc[a][0] = a01.x, acc[a][1] = a01.y, acc[a][2] = a23.x, acc[a][3] = a23.y;
                 }
             }
         }
