@@ -17,13 +17,11 @@
 // Layout: thread t owns the contiguous logits [16 t, 16 t + 16) (four float4
 // loads), thread 511 also the start and stop codes 8192 and 8193, so index-
 // ordered compaction is one block scan.  The k-th largest score is found by a
-// radix select on order-preserving integer keys: a 10-bit first digit, then a
-// direct ranking of the (usually few dozen) keys in the selected bin, or 8-bit
-// passes when that bin is crowded; the top-p survivors are sorted with a
-// bitonic sort of 64-bit (score key, index) words (within one warp for up to
-// 32); the double-precision sums that fix the reference's rounding order run
-// sequentially in thread 0 over values computed in parallel, and one warp
-// searches the running sums.
+// 4-pass 8-bit radix select on order-preserving integer keys with warp-
+// aggregated histogram updates; the top-p survivors are sorted with a bitonic
+// sort of 64-bit (score key, index) words (within one warp for up to 32); the
+// double-precision sums that fix the reference's rounding order run
+// sequentially in thread 0 over values computed in parallel.
 #pragma once
 
 #include "common.cuh"
@@ -39,15 +37,8 @@ constexpr int kBits = (kVocab + 31) / 32;
 constexpr int kSortCap = 16384;  // next power of two >= 8194
 constexpr int kFast = 256;       // survivors handled entirely in shared memory
 
-constexpr int kSelBits = 10;                // first radix digit of the k-th largest search
-constexpr int kSelBins = 1 << kSelBits;
-constexpr int kCand = 512;                  // candidates ranked directly after that digit
-static_assert(kSelBins == 2 * kThreads, "two first-digit bins per thread");
-
-// Shared-memory part (~11.4 KB).  Up to kFast survivors are gathered, sorted and
-// their exp() values cached here; larger survivor sets use SamplerBig.  The
-// k-th largest search runs before any survivor is gathered, so its histogram
-// and candidate list share the survivor arrays' space.
+// Shared-memory part (~9.7 KB).  Up to kFast survivors are gathered, sorted and
+// their exp() values cached here; larger survivor sets use SamplerBig.
 struct SamplerSmem {
     uint32_t seen[kBits];
     uint32_t removed[kBits];
@@ -55,24 +46,15 @@ struct SamplerSmem {
     uint32_t scan[32];
     float redf[32];
     uint32_t redu[32];
-    uint32_t sel_bin, sel_rem, result, n_cand;
+    uint32_t sel_bin, sel_rem, result;
     int err;
     double f_total;
-    union {
-        struct {
-            uint32_t idx[kFast];
-            float s[kFast];
-            unsigned long long key[kFast];
-            double pr[kFast];
-            double q[kFast];  // top-p: exp / total in ascending order, then its running sums
-        } f;
-        struct {
-            uint32_t hist[kSelBins];  // counts of the first digit (key >> 22)
-            uint32_t cand[kCand];     // keys in the selected bin
-        } sel;
-    } u;
+    uint32_t f_idx[kFast];
+    float f_s[kFast];
+    unsigned long long f_key[kFast];
+    double f_pr[kFast];
+    double f_q[kFast];  // top-p: exp / total in ascending order
 };
-static_assert(sizeof(SamplerSmem::u.sel) <= sizeof(SamplerSmem::u.f), "selection scratch inside the survivor arrays");
 
 // Workspace for more than kFast survivors (top-p without top-k, or wide ties):
 // shared memory in single-CTA kernels, a per-CTA global slice in the
@@ -178,88 +160,36 @@ __device__ inline uint32_t block_excl_scan(uint32_t v, SamplerSmem& sm, uint32_t
 }
 
 // Value of the kk-th largest element (with multiplicity) over the CTA's
-// scores, i.e. sorted-descending[kk-1] of std::nth_element.  Radix select on
-// the order-preserving keys: one 10-bit digit (1024 bins, descending counts
-// scanned by the whole CTA), then, when the selected bin holds at most kCand
-// keys (the usual case: a few dozen), each of them is ranked against the
-// others directly; otherwise 8-bit passes over the remaining bits finish the
-// search.
+// scores, i.e. sorted-descending[kk-1] of std::nth_element.
 __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk, SamplerSmem& sm) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int kShift = 32 - kSelBits;
-    uint32_t* hist = sm.u.sel.hist;
-    hist[2 * tid] = 0;
-    hist[2 * tid + 1] = 0;
-    csync();
-#pragma unroll
-    for (int k = 0; k < kPer; ++k)
-        if (k < cnt) atomicAdd(&hist[ord_key(s[k]) >> kShift], 1u);
-    csync();
-    {
-        // thread t holds bins 1023 - 2t (higher) and 1022 - 2t: thread order is descending bin order
-        const uint32_t hi = hist[kSelBins - 1 - 2 * tid], lo = hist[kSelBins - 2 - 2 * tid];
-        uint32_t total;
-        const uint32_t before = block_excl_scan(hi + lo, sm, &total);
-        if (before < kk && kk <= before + hi + lo) {
-            const bool in_hi = kk <= before + hi;
-            sm.sel_bin = uint32_t(kSelBins - (in_hi ? 1 : 2) - 2 * tid);
-            sm.sel_rem = kk - before - (in_hi ? 0u : hi);
-        }
-        if (tid == 0) sm.n_cand = 0;
-        csync();
-    }
-    const uint32_t bin = sm.sel_bin, c = hist[bin];
-    uint32_t rem = sm.sel_rem;
-    if (c <= (uint32_t)kCand) {
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const uint32_t key = ord_key(s[k]);
-            if (k < cnt && (key >> kShift) == bin) sm.u.sel.cand[atomicAdd(&sm.n_cand, 1u)] = key;
-        }
-        csync();
-        for (uint32_t i = tid; i < c; i += kThreads) {
-            const uint32_t x = sm.u.sel.cand[i];
-            uint32_t gt = 0, ge = 0;
-            for (uint32_t j = 0; j < c; ++j) {
-                const uint32_t y = sm.u.sel.cand[j];
-                gt += y > x;
-                ge += y >= x;
-            }
-            if (gt < rem && rem <= ge) sm.result = x;  // equal keys write the same value
-        }
-        csync();
-        const uint32_t key = sm.result;
-        csync();
-        return key_float(key);
-    }
-    uint32_t prefix = bin << kShift, mask = ~0u << kShift;
-    // 8-bit passes over bits 14..21 and 6..13, then 0..7 (bits 6 and 7 are
-    // already fixed for every participant, so the last bin is consistent)
-    for (int pass = 0; pass < 3; ++pass) {
-        const int shift = pass == 0 ? 14 : pass == 1 ? 6 : 0;
-        for (int i = tid; i < 256; i += kThreads) sm.hist[i] = 0;
+    uint32_t prefix = 0, mask = 0, rem = kk;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = threadIdx.x; i < 256; i += kThreads) sm.hist[i] = 0;
         csync();
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
             const uint32_t key = ord_key(s[k]);
             const bool part = k < cnt && (key & mask) == prefix;
-            const uint32_t b = (key >> shift) & 255u;
+            const uint32_t bin = (key >> shift) & 255u;
             const unsigned act = __ballot_sync(0xffffffffu, part);
-            if (act) {  // the lanes sharing the first participant's bin add with one atomic; the rest singly
+            if (act) {  // the lanes sharing the first participant's bin (most of them, as scores
+                        // cluster in a few high-order bins) add with one atomic; the rest singly
                 const int leader = __ffs(act) - 1;
-                const uint32_t lb = __shfl_sync(0xffffffffu, b, leader);
-                const unsigned same = __ballot_sync(0xffffffffu, part && b == lb);
+                const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
+                const unsigned same = __ballot_sync(0xffffffffu, part && bin == lb);
                 if (lane == leader) atomicAdd(&sm.hist[lb], (uint32_t)__popc(same));
-                if (part && b != lb) atomicAdd(&sm.hist[b], 1u);
+                if (part && bin != lb) atomicAdd(&sm.hist[bin], 1u);
             }
         }
         csync();
         if (warp == 0) {
-            uint32_t cc[8], sum = 0;
+            uint32_t c[8], sum = 0;
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                cc[e] = sm.hist[255 - 8 * lane - e];
-                sum += cc[e];
+                c[e] = sm.hist[255 - 8 * lane - e];
+                sum += c[e];
             }
             uint32_t inc = sum;
 #pragma unroll
@@ -272,12 +202,12 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
             if (lane == tl) {
                 uint32_t acc = inc - sum;
                 for (int e = 0; e < 8; ++e) {
-                    if (acc + cc[e] >= rem) {
+                    if (acc + c[e] >= rem) {
                         sm.sel_bin = 255u - 8u * lane - e;
                         sm.sel_rem = rem - acc;
                         break;
                     }
-                    acc += cc[e];
+                    acc += c[e];
                 }
             }
         }
@@ -288,25 +218,6 @@ __device__ inline float kth_largest(const float (&s)[kPer], int cnt, uint32_t kk
         csync();
     }
     return key_float(prefix);
-}
-
-// First (or, with `last`, final) position i < n, scanned by warp 0 in order,
-// where pred(i) holds; n when there is none.  n <= kFast.
-template <bool kLast, class P>
-__device__ __forceinline__ uint32_t warp_find(uint32_t n, P pred) {
-    const int lane = threadIdx.x & 31;
-    constexpr int kPerLane = kFast / 32;
-    uint32_t hit = 0;  // bit e: position kPerLane * lane + e
-#pragma unroll
-    for (int e = 0; e < kPerLane; ++e) {
-        const uint32_t i = kPerLane * lane + e;
-        if (i < n && pred(i)) hit |= 1u << e;
-    }
-    const unsigned ball = __ballot_sync(0xffffffffu, hit != 0);
-    if (!ball) return n;
-    const int l = kLast ? 31 - __clz(ball) : __ffs(ball) - 1;
-    const uint32_t h = __shfl_sync(0xffffffffu, hit, l);
-    return kPerLane * l + (kLast ? 31 - __clz(h) : __ffs(h) - 1);
 }
 
 // Ascending sort of key[0..32) by warp 0 in registers; the caller publishes
@@ -454,10 +365,10 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
     uint32_t n = 0;
     uint32_t off = block_excl_scan(nf, sm, &n);
     const bool fast = n <= (uint32_t)kFast;
-    uint32_t* idx = fast ? sm.u.f.idx : big->sv_idx;
-    float* sc = fast ? sm.u.f.s : big->sv_s;
-    unsigned long long* key = fast ? sm.u.f.key : big->key;
-    double* pr = fast ? sm.u.f.pr : nullptr;
+    uint32_t* idx = fast ? sm.f_idx : big->sv_idx;
+    float* sc = fast ? sm.f_s : big->sv_s;
+    unsigned long long* key = fast ? sm.f_key : big->key;
+    double* pr = fast ? sm.f_pr : nullptr;
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
         if (k < cnt && isfinite(s[k])) {
@@ -507,26 +418,22 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
         csync();
         if (pr && !sm.err) {
             // each survivor's share in ascending order (the reference's division),
-            // then the cumulative mass by one thread in that order (every running
-            // sum kept, so the loads pipeline), then the count of leading
-            // survivors whose mass stays <= 1 - p found by one warp, removed in
-            // parallel (cumulative mass only grows: nothing later is removed)
+            // then the cumulative mass by one thread in that order: the count of
+            // leading survivors whose mass stays <= 1 - p, removed in parallel
             const double total = sm.f_total;
-            for (uint32_t j = tid; j < n; j += kThreads) sm.u.f.q[j] = pr[uint32_t(key[j])] / total;
+            for (uint32_t j = tid; j < n; j += kThreads) sm.f_q[j] = pr[uint32_t(key[j])] / total;
             csync();
             if (tid == 0) {
+                const double low = 1.0 - double(o.top_p);
                 double cum = 0.0;
+                uint32_t nrem = 0;
 #pragma unroll 8
                 for (uint32_t j = 0; j < n; ++j) {
-                    cum += sm.u.f.q[j];
-                    sm.u.f.q[j] = cum;
+                    cum += sm.f_q[j];
+                    if (!(cum <= low)) break;  // cumulative mass only grows: nothing later is removed
+                    nrem = j + 1;
                 }
-            }
-            csync();
-            if (tid < 32) {
-                const double low = 1.0 - double(o.top_p);
-                const uint32_t nrem = warp_find<false>(n, [&](uint32_t j) { return !(sm.u.f.q[j] <= low); });
-                if (tid == 0) sm.sel_rem = nrem;
+                sm.sel_rem = nrem;
             }
             csync();
             for (uint32_t j = tid; j < sm.sel_rem; j += kThreads) {
@@ -548,7 +455,7 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
                 double cum = 0.0;
                 for (uint32_t j = 0; j < n; ++j) {
                     const uint32_t pos = uint32_t(key[j]);
-                    cum += pr ? sm.u.f.q[j] : exp(double(sc[pos] - mx)) / total;
+                    cum += pr ? sm.f_q[j] : exp(double(sc[pos] - mx)) / total;
                     if (cum <= low) {
                         const uint32_t t = idx[pos];
                         sm.removed[t >> 5] |= 1u << (t & 31);
@@ -584,37 +491,34 @@ __device__ inline uint32_t run_sampler(const float* logits, const SampleOpts& o,
     // CDF sample in index order (double precision).  The maximum is unchanged
     // by top-p (the top score is always kept).  With the survivors' exp values
     // cached, the mass of each survivor (0 when removed) is gathered in
-    // parallel and one thread folds it in index order as the reference does,
-    // keeping every running sum (in place of the exp values, no longer
-    // needed).  Adding a zero mass leaves a sum unchanged, so the running sum
-    // at i is the reference's `cum` there, and the first i with target < sum
-    // has a non-zero mass: one warp finds it, or the reference's fallback, the
-    // last survivor with non-zero mass.
+    // parallel and one thread folds it in index order as the reference does.
     if (pr) {
         csync();
-        for (uint32_t i = tid; i < n; i += kThreads) sm.u.f.q[i] = bit_get(sm.removed, idx[i]) ? 0.0 : pr[i];
+        for (uint32_t i = tid; i < n; i += kThreads) sm.f_q[i] = bit_get(sm.removed, idx[i]) ? 0.0 : pr[i];
         csync();
         if (tid == 0) {
             double total = 0.0;
 #pragma unroll 8
-            for (uint32_t i = 0; i < n; ++i) {
-                total += sm.u.f.q[i];
-                pr[i] = total;
+            for (uint32_t i = 0; i < n; ++i) total += sm.f_q[i];
+            if (!(total > 0.0)) {
+                set_status(status, kStatusZeroMass, 102, 0);
+                sm.result = 0xffffffffu;
+            } else {
+                const double target = uniform_at(o.rng, o.seed, draw) * total;
+                double cum = 0.0;
+                uint32_t last = 0, pick = 0xffffffffu;
+                for (uint32_t i = 0; i < n; ++i) {
+                    const double p = sm.f_q[i];
+                    if (p <= 0.0) continue;
+                    last = i;
+                    cum += p;
+                    if (target < cum) {
+                        pick = i;
+                        break;
+                    }
+                }
+                sm.result = idx[pick == 0xffffffffu ? last : pick];
             }
-            sm.err = total > 0.0 ? 0 : kStatusZeroMass;
-            if (sm.err) set_status(status, kStatusZeroMass, 102, 0);
-            else sm.f_total = uniform_at(o.rng, o.seed, draw) * total;
-        }
-        csync();
-        if (tid < 32) {
-            uint32_t r = 0xffffffffu;
-            if (!sm.err) {
-                const double target = sm.f_total;
-                uint32_t pick = warp_find<false>(n, [&](uint32_t i) { return target < pr[i]; });
-                if (pick == n) pick = warp_find<true>(n, [&](uint32_t i) { return sm.u.f.q[i] > 0.0; });
-                r = idx[pick];
-            }
-            if (tid == 0) sm.result = r;
         }
         csync();
         return sm.result;
