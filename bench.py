@@ -15,6 +15,12 @@ weights seed 42, stop code masked so every request runs to its length):
                     as config 1), longest-first over the ranks, each rank
                     serving its share with continuous batching (itts_gpt_serve,
                     16 rows in flight).
+  --config qwen     the Qwen3-0.6B emotion-text decoder (src/qwen.cpp): a
+                    180-id prompt, greedy generate(128) to EOS; tokens/s.
+  --config codec    the semantic codec's decode (src/codec.cpp:50-69) of the
+                    1024 codes of a configs[1] request; codes/s.
+  --prefill-profile one prefill of the config's prefix between
+                    cudaProfilerStart/Stop (profiler captures only).
 Multi-GPU: one replica per GPU (weights replicated, no collective on the data
 path; NCCL only for the start/stop barriers and the max-over-ranks time).
 
