@@ -16,9 +16,13 @@
 // (kernels.metal:1397-1425 sums over in_c, then k); the final convolution's
 // window reads the nearest-upsampled rows x[floor(s / 2)] directly
 // (kernels.metal:1376-1395 with scale in/out = 0.5).  Epilogues fuse the bias,
-// the GELU of pwconv1 and the layer scale + residual of pwconv2.  fp32 on the
-// CUDA cores, 64 x 64 tiles, k-tiles of 32; each output sums its K products in
-// k order.
+// the GELU of pwconv1 and the layer scale + residual of pwconv2.  Two GEMM
+// paths: by default the TMA-fed tcgen05 GEMM of gemm_tma.cu on TF32 hi / lo
+// operands (the convolutions' windows written out as split im2col rows, the
+// activations that feed a GEMM split by the kernel producing them, the chain
+// launched with PDL); in GEMM mode 1 fp32 on the CUDA cores (k_codec_gemm,
+// 64 x 64 tiles, k-tiles of 32, each output summing its K products in k
+// order, reading the windows directly).
 #include <vector>
 
 #include "codec.hpp"
