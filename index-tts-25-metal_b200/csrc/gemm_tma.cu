@@ -1,6 +1,9 @@
-// Prefill linears of the fp32-weight path on the 5th-generation tensor cores
-// (tcgen05, sm_100a), fed by TMA:
+// The fp32-accuracy GEMMs of the GPT prefill, the semantic codec's decode and
+// the Qwen3 prompt pass on the 5th-generation tensor cores (tcgen05, sm_100a),
+// fed by TMA:
 //   C[m, n] = epi(sum_k A[m, k] * W[n, k] + bias[n]),   A [M, K], W [N, K]
+// epilogues: bias; GELU (tanh form) or GELU (erf form), optionally split into
+// hi / lo for the next GEMM; residual; layer scale + residual; SwiGLU.
 //
 // Accuracy.  Every operand x is held as two TF32-exact fp32 words,
 // hi = rn_tf32(x) and lo = rn_tf32(x - hi) (x - hi is exact in fp32), so
@@ -16,8 +19,10 @@
 // context is created (k_split_tf32); the activations by the kernel that
 // produces them (LayerNorm, attention, the GELU epilogue of c_fc).
 //
-// Tiling.  One CTA per 128 x 128 output tile (optionally one K range of it:
-// split K), 320 threads in three roles:
+// Tiling.  128 x 128 output tiles shared out stream-K: the (tile, 32-wide K
+// block) units are split evenly over up to one CTA per SM, so a CTA may own
+// part of a tile; when the tiles number between 3/4 of the SMs and all of
+// them, one CTA per whole tile.  320 threads in three roles:
 //   warp 0 (one lane)  TMA producer: per 32-wide K block, four 2-D tensor
 //                      loads (A hi, A lo: 128 rows; W hi, W lo: 128 rows) of
 //                      128-byte rows into a kStages-deep ring of 64 KB stages,
@@ -34,10 +39,12 @@
 //                      of the columns, adds each chunk into 64 fp32
 //                      registers, then applies bias and
 //                      GELU (split into hi / lo for the next GEMM) or the
-//                      residual.  With split K every CTA stores its partial
-//                      tile; the last to arrive (per-tile counter) sums the
-//                      partials in split order, so results do not depend on
-//                      which CTA finishes last.
+//                      residual.  A tile split between CTAs: every CTA
+//                      stores its partial tile; the last to arrive (per-tile
+//                      counter) sums the partials in CTA order, so results do
+//                      not depend on which CTA finishes last.
+// Launched with programmatic stream serialization: the producer requests the
+// first stages' weight tiles before waiting for the previous kernel.
 // Every mbarrier wait is bounded by time; a CTA that gives up records a status,
 // waits (bounded) for its own TMA loads and MMAs, frees its tensor memory and
 // returns without writing its tile.

@@ -3,9 +3,10 @@
 // T <= 1024 rows.  Per layer: LayerNorm rows, the QKV GEMM, the K/V store into
 // the cache (head-major layout), causal attention, c_proj GEMM with the
 // residual fused, LayerNorm, c_fc GEMM with GELU fused, mlp.c_proj GEMM with
-// the residual fused.  GEMMs are C[T, N] = A[T, K] . W[N, K]^T in fp32 on the
-// CUDA cores (64x64 tiles, double-buffered shared memory), which keeps fp32
-// parity with the reference's MPS fp32 GEMMs (metal_context.mm:368-410).
+// the residual fused.  GEMMs are C[T, N] = A[T, K] . W[N, K]^T with fp32
+// accuracy (the reference's MPS fp32 GEMMs, metal_context.mm:368-410): by
+// default on the tensor cores (gemm_tma.cu, TF32 hi / lo operands, the chain
+// launched with PDL); in prefill mode 1 on the CUDA cores (k_gemm_nt below).
 #include "common.cuh"
 #include "model.hpp"
 
